@@ -1,0 +1,406 @@
+"""Benchmark: paged-decode HBM TB/s (and prefill TFLOP/s) vs the B200 roofline.
+
+Default workload (the one quoted at 1/2/4/8 GPUs):
+long-context FP8 E4M3 paged decode with split-KV. 64 requests x 131072 cached
+tokens, page 16, 32 query / 8 KV heads, head_dim 128. The cache is built by
+store_kvcache from seeded N(0,1) bf16 rows with per-head scales U[1/448,4/448]
+through a seeded slot_mapping over randomly permuted pages. With N GPUs the KV
+sequence is sharded: rank r owns tokens [r*C/N, (r+1)*C/N) of every request in
+its own page pool; each rank decodes its shard to an fp32 partial (out, LSE),
+the partials are all-gathered with NCCL and merged by the merge kernel.
+
+`value` = algorithmic bytes of one decode step (every cached K/V byte read once
+plus tables, q and out) / max-over-ranks device time per step (strong scaling).
+`e2e` = the same bytes / the time of a full serving step through the public API
+with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
+that token, attention, D2H of the output.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload fp8_decode|decode|prefill]
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "flash-attn-mps_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "paged-decode HBM TB/s & prefill TFLOP/s vs B200 roofline at 1/2/4/8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+def dist_setup(n_gpus):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(value, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------ config 4 setup
+CFG4 = dict(batch=64, ctx=131072, page=16, hq=32, hkv=8, d=128)
+
+
+def build_fp8_cache(rank, world, cfg, seed=4):
+    """This rank's shard of the config-4 FP8 paged cache, built by store_kvcache."""
+    import torch
+    from flash_attn_b200 import store_kvcache
+    B, C, P, HK, D = cfg["batch"], cfg["ctx"], cfg["page"], cfg["hkv"], cfg["d"]
+    shard = C // world
+    pages_per_req = shard // P
+    n_pages = B * pages_per_req
+    dev = torch.device("cuda")
+    gen = torch.Generator(device="cpu").manual_seed(seed * 1000 + rank)
+    perm = torch.randperm(n_pages, generator=gen).to(torch.int32)
+    table = perm.reshape(B, pages_per_req).to(dev)
+    ks = ((1 + 3 * torch.rand(HK, generator=gen)) / 448).to(dev)
+    vs = ((1 + 3 * torch.rand(HK, generator=gen)) / 448).to(dev)
+    k_cache = torch.empty(n_pages, P, HK, D, dtype=torch.float8_e4m3fn, device=dev)
+    v_cache = torch.empty_like(k_cache)
+    g = torch.Generator(device=dev).manual_seed(seed * 1000 + rank + 7)
+    chunk_req = max(1, (1 << 20) // shard)
+    pos = torch.arange(shard, device=dev)
+    for b0 in range(0, B, chunk_req):
+        b1 = min(B, b0 + chunk_req)
+        n = (b1 - b0) * shard
+        k = torch.randn(n, HK, D, device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        v = torch.randn(n, HK, D, device=dev, generator=g, dtype=torch.float32).to(torch.bfloat16)
+        slots = (table[b0:b1, pos // P].long() * P + (pos % P)).reshape(-1)
+        store_kvcache(k, v, k_cache, v_cache, slots, k_scale=ks, v_scale=vs)
+        del k, v
+    torch.cuda.synchronize()
+    return k_cache, v_cache, table, ks, vs
+
+
+def cfg4_bytes(cfg):
+    B, C, HK, D, HQ = cfg["batch"], cfg["ctx"], cfg["hkv"], cfg["d"], cfg["hq"]
+    kv = B * C * HK * 2 * D * 1
+    table = B * (C // cfg["page"]) * 4
+    qo = 2 * B * HQ * D * 2
+    return kv + table + qo
+
+
+def run_fp8_decode(args, rank, world, peaks, peak_kind):
+    import torch
+    import torch.distributed as dist
+    from flash_attn_b200 import store_kvcache
+    from flash_attn_b200._attention import attention
+    from flash_attn_b200._merge import _merge_partials
+
+    cfg = dict(CFG4)
+    B, C, HQ, HK, D = cfg["batch"], cfg["ctx"], cfg["hq"], cfg["hkv"], cfg["d"]
+    shard = C // world
+    dev = torch.device("cuda")
+    k_cache, v_cache, table, ks, vs = build_fp8_cache(rank, world, cfg)
+    gq = torch.Generator(device="cpu").manual_seed(99)
+    q_host = torch.randn(B, HQ, D, generator=gq).to(torch.bfloat16).pin_memory()
+    q = q_host.to(dev)
+    kd = ks.reshape(1, HK).expand(B, HK)
+    vd = vs.reshape(1, HK).expand(B, HK)
+    cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    used = torch.full((B,), shard, dtype=torch.int32, device=dev)
+    sinks = None
+    partial = torch.empty(B, HQ, D, dtype=torch.float32, device=dev)
+    gathered = torch.empty(world, B, HQ, D, dtype=torch.float32, device=dev)
+    gathered_lse = torch.empty(world, HQ, B, dtype=torch.float32, device=dev)
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+    out_lse = torch.empty(HQ, B, dtype=torch.float32, device=dev)
+
+    def step(q_in):
+        if world == 1:
+            return attention(q_in, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
+                             max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
+                             s_aux=sinks, out=out)
+        o, l = attention(q_in, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
+                         max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
+                         out=partial)
+        dist.all_gather_into_tensor(gathered.view(world, -1), o.reshape(-1))
+        dist.all_gather_into_tensor(gathered_lse.view(world, -1), l.reshape(-1))
+        return _merge_partials(gathered, gathered_lse, out=out, out_lse=out_lse)
+
+    # ---- device-resident timing --------------------------------------------
+    for _ in range(args.warmup):
+        step(q)
+    barrier(world)
+    sampler = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    start.record(stream)
+    for _ in range(args.steps):
+        step(q)
+    end.record(stream)
+    barrier(world)
+    ms = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms, world)
+
+    # ---- dominant kernel alone: the local decode operation (decode + split merge)
+    k_start, k_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    k_start.record(stream)
+    for _ in range(args.steps):
+        attention(q, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
+                  max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
+                  out=partial if world > 1 else out)
+    k_end.record(stream)
+    barrier(world)
+    kernel_ms = max_over_ranks(k_start.elapsed_time(k_end) / args.steps, world)
+    clocks = sampler.stop() if sampler else None
+
+    # ---- end to end through the public API with host buffers ----------------
+    new_k_host = torch.randn(B, HK, D, generator=gq).to(torch.bfloat16).pin_memory()
+    new_v_host = torch.randn(B, HK, D, generator=gq).to(torch.bfloat16).pin_memory()
+    out_host = torch.empty(B, HQ, D, dtype=torch.bfloat16).pin_memory()
+    # The new token replaces the last cached position, keeping the context fixed.
+    last = shard - 1
+    slots = (table[:, last // cfg["page"]].long() * cfg["page"] + last % cfg["page"]).contiguous()
+    is_last_rank = rank == world - 1
+
+    def e2e_step():
+        qd = q_host.to(dev, non_blocking=True)
+        if is_last_rank:
+            nk = new_k_host.to(dev, non_blocking=True)
+            nv = new_v_host.to(dev, non_blocking=True)
+            store_kvcache(nk, nv, k_cache, v_cache, slots, k_scale=ks, v_scale=vs)
+        o = step(qd)
+        result = o[0] if isinstance(o, tuple) else o
+        out_host.copy_(result, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier(world)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.steps, world)
+
+    total_bytes = cfg4_bytes(cfg)
+    rank_bytes = total_bytes / world
+    value = total_bytes / (ms * 1e-3) / 1e12
+    achieved_gbs = rank_bytes / (kernel_ms * 1e-3) / 1e9
+    result = {
+        "value": value, "unit": "TB/s", "ms_per_step": ms,
+        "e2e": {"value": total_bytes / (e2e_ms * 1e-3) / 1e12, "unit": "TB/s",
+                "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": q_host.numel() * 2 + (new_k_host.numel() + new_v_host.numel()) * 2,
+                "d2h_bytes_per_step": out_host.numel() * 2},
+        "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel (+ its split merge)",
+                     "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved_gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)",
+                     "traffic": None, "algorithmic_bytes_per_launch": rank_bytes,
+                     "kernel_ms": kernel_ms},
+        "dtype": "fp8_e4m3 KV / bf16 q, fp32 softmax",
+        "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode, split-KV, KV sharded over ranks",
+                   "batch": B, "context": C, "block_size": cfg["page"], "q_heads": HQ, "kv_heads": HK,
+                   "head_dim": D, "kv_bytes_total": B * C * HK * 2 * D,
+                   "l2": "inputs (17.2 GB cache) larger than L2; no flush needed",
+                   "parallelism": f"kv-seq sharded x{world} + NCCL all-gather + merge"},
+        "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "clocks": clocks,
+    }
+    return result
+
+
+# ------------------------------------------------------------------ CPU legs
+def cpu_fp8_decode_sample(cfg, requests=1, seed=4):
+    """The oracle (reference CPU math, float64) on a bounded sample of config 4."""
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(seed)
+    C, HQ, HK, D = cfg["ctx"], cfg["hq"], cfg["hkv"], cfg["d"]
+    codes_k = rng.integers(0, 256, size=(requests * C, HK, D), dtype=np.uint8)
+    codes_v = rng.integers(0, 256, size=(requests * C, HK, D), dtype=np.uint8)
+    codes_k[(codes_k & 0x7F) == 0x7F] = 0  # no NaN codes
+    codes_v[(codes_v & 0x7F) == 0x7F] = 0
+    q = rng.standard_normal((requests, HQ, D))
+    cu_q = np.arange(requests + 1)
+    cu_k = np.arange(requests + 1) * C
+    desc = np.full((requests, HK), 1 / 112.0)
+    t0 = time.perf_counter()
+    k = oracle.e4m3_decode(codes_k)
+    v = oracle.e4m3_decode(codes_v)
+    oracle.attention(q, k, v, cu_q, cu_k=cu_k, k_descale=desc, v_descale=desc)
+    dt = time.perf_counter() - t0
+    nbytes = requests * C * HK * 2 * D
+    return nbytes / dt / 1e12, dt, f"{requests} request(s) x {C} tokens of config 4 (FP8 decode + float64 attention)"
+
+
+def cpu_baseline_block(cfg):
+    import numpy as np  # noqa: F401
+    value, dt, sample = cpu_fp8_decode_sample(cfg)
+    return {"value": value, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": sample, "seconds": dt}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU math path (oracle port) on host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    cfg = dict(CFG4)
+    times = []
+    for _ in range(args.warmup):
+        cpu_fp8_decode_sample(cfg)
+    for _ in range(args.steps):
+        value, dt, sample = cpu_fp8_decode_sample(cfg)
+        times.append(dt)
+    ms = statistics.median(times) * 1e3
+    nbytes = cfg["ctx"] * cfg["hkv"] * 2 * cfg["d"]
+    value = nbytes / (ms * 1e-3) / 1e12
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp8_e4m3 KV decoded to float64", "data": "synthetic",
+        "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode (bounded CPU sample per step)",
+                   "batch": cfg["batch"], "context": cfg["ctx"], "q_heads": cfg["hq"],
+                   "kv_heads": cfg["hkv"], "head_dim": cfg["d"]},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["fp8_decode"], default="fp8_decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line))
+        return
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    peaks, peak_kind = load_peaks()
+    res = run_fp8_decode(args, rank, world, peaks, peak_kind)
+    if rank == 0:
+        line = {"metric": METRIC, "value": res["value"], "unit": res["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"],
+                "e2e": res["e2e"], "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
+                "clocks": res["clocks"]}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_block(CFG4)
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

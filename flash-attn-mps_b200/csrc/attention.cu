@@ -1,0 +1,267 @@
+// Attention dispatch (host side of the C ABI): argument checks, kernel choice,
+// split-KV planning and the partial merge.
+//
+// Routing follows the reference dispatcher (flash_attn_mps/_attention.py:170-320):
+//   * one query per request, not deterministic, no ALiBi, no mask
+//     -> decode (_attention.py:216-229 -> _decode.py:40-99): the tensor-core
+//        decode kernel when its envelope fits, else the generic kernel;
+//   * eligible dense/varlen prefill -> the tcgen05 kernel (the reference's
+//     "fast" predicate, _attention.py:231-240);
+//   * everything else -> the generic kernel with the reference's split rule
+//     (_attention.py:241-243).
+// The choice depends on shapes, dtypes, strides and flags only, never on
+// tensor values or lengths beyond the caller's max_seqlen_*.
+#include "kernels.cuh"
+
+namespace fab {
+
+std::string& last_error() {
+  thread_local std::string message;
+  return message;
+}
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  last_error() = buf;
+  return code;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+namespace {
+
+enum Route { kRouteGeneric = 0, kRouteDecode = 1, kRoutePrefill = 2 };
+
+struct Plan {
+  int route;
+  int splits;
+  int span;          // decode only
+  size_t part_bytes, lse_bytes;
+};
+
+int validate(const fa_attention_args* a) {
+  FAB_CHECK_ARG(a != nullptr, "null arguments");
+  const fa_tensor &q = a->q, &k = a->k, &v = a->v;
+  FAB_CHECK_ARG(present(q) && present(k) && present(v) || q.shape[0] == 0,
+                "q, k and v are required");
+  FAB_CHECK_ARG(q.ndim == 3 && (k.ndim == 3 || k.ndim == 4) && v.ndim == k.ndim,
+                "q must be packed 3-D; k/v must be packed 3-D or paged 4-D");
+  for (const fa_tensor* t : {&q, &k, &v})
+    FAB_CHECK_ARG(t->dtype == FA_F16 || t->dtype == FA_BF16 || t->dtype == FA_F32 || t->dtype == FA_E4M3,
+                  "attention supports FP16, BF16, FP32 and FP8 E4M3FN");
+  const int64_t dq = q.shape[2], dv = v.shape[v.ndim - 1];
+  FAB_CHECK_ARG(dq >= 1 && dq <= 512 && dv >= 1 && dv <= 512,
+                "query/key and value head dimensions must be in 1..512");
+  for (int i = 0; i < k.ndim - 1; ++i)
+    FAB_CHECK_ARG(k.shape[i] == v.shape[i], "key/value shapes must agree except for their last dimension");
+  FAB_CHECK_ARG(k.shape[k.ndim - 1] == dq, "key/value shapes must agree except for their last dimension");
+  const int64_t heads = q.shape[1], kh = k.shape[k.ndim - 2];
+  FAB_CHECK_ARG(heads >= 1 && kh >= 1 && heads % kh == 0, "query heads must be a positive multiple of KV heads");
+  FAB_CHECK_ARG((k.ndim == 4) == present(a->block_table),
+                "paged 4-D KV requires block_table; packed 3-D KV does not");
+  FAB_CHECK_ARG(present(a->cu_seqlens_k) || present(a->seqused_k), "cu_seqlens_k or seqused_k is required");
+  FAB_CHECK_ARG(a->num_splits >= 0, "num_splits must be nonnegative");
+  FAB_CHECK_ARG(present(a->out) && a->out.ndim == 3 && a->out.shape[0] == q.shape[0] &&
+                    a->out.shape[1] == heads && a->out.shape[2] == dv,
+                "out must have shape [total_q, query_heads, value_dim]");
+  FAB_CHECK_ARG(is_float(a->out.dtype), "out must have FP16, BF16 or FP32 dtype");
+  FAB_CHECK_ARG(present(a->lse) && a->lse.ndim == 2 && a->lse.dtype == FA_F32 &&
+                    a->lse.shape[0] == heads && a->lse.shape[1] == q.shape[0],
+                "lse must be float32 [heads, total_q]");
+  if (q.shape[0] == 0) return FA_OK;
+  FAB_CHECK_ARG(a->max_seqlen_q > 0 && a->max_seqlen_k >= 0,
+                "nonempty q requires positive max_seqlen_q and nonnegative max_seqlen_k");
+  FAB_CHECK_ARG(a->batch >= 1 && present(a->cu_seqlens_q) && a->cu_seqlens_q.dtype == FA_I32 &&
+                    a->cu_seqlens_q.shape[0] == a->batch + 1,
+                "cu_seqlens_q must contain at least two offsets");
+  if (present(a->block_table))
+    FAB_CHECK_ARG(a->block_table.dtype == FA_I32 && a->block_table.ndim == 2, "block_table must be int32 [B,P]");
+  FAB_CHECK_ARG(a->mask_kind >= 0 && a->mask_kind <= 2, "unknown mask kind");
+  if (a->mask_kind == 1)
+    FAB_CHECK_ARG(present(a->mask_aux0) && a->mask_aux0.ndim == 2, "mask kind 1 needs query ranges [T,2]");
+  if (a->mask_kind == 2)
+    FAB_CHECK_ARG(present(a->mask_aux0) && present(a->mask_aux1), "mask kind 2 needs prefix and window");
+  return FA_OK;
+}
+
+void fill_params(const fa_attention_args* a, AttnParams* p) {
+  *p = AttnParams{};
+  const fa_tensor &q = a->q, &k = a->k, &v = a->v;
+  p->q = q.ptr; p->k = k.ptr; p->v = v.ptr;
+  p->qt = q.dtype; p->kt = k.dtype; p->vt = v.dtype;
+  p->qs0 = q.stride[0]; p->qs1 = q.stride[1]; p->qs2 = q.stride[2];
+  if (k.ndim == 4) {
+    p->ks0 = k.stride[0]; p->ks1 = k.stride[1]; p->ks2 = k.stride[2]; p->ks3 = k.stride[3];
+    p->vs0 = v.stride[0]; p->vs1 = v.stride[1]; p->vs2 = v.stride[2]; p->vs3 = v.stride[3];
+    p->page = (int32_t)k.shape[1];
+    p->paged = 1;
+  } else {
+    p->ks1 = k.stride[0]; p->ks2 = k.stride[1]; p->ks3 = k.stride[2];
+    p->vs1 = v.stride[0]; p->vs2 = v.stride[1]; p->vs3 = v.stride[2];
+  }
+  p->out = a->out.ptr; p->ot = a->out.dtype;
+  p->os0 = a->out.stride[0]; p->os1 = a->out.stride[1]; p->os2 = a->out.stride[2];
+  p->lse = reinterpret_cast<float*>(a->lse.ptr);
+  p->ls0 = a->lse.stride[0]; p->ls1 = a->lse.stride[1];
+  p->cu_q = reinterpret_cast<const int32_t*>(a->cu_seqlens_q.ptr); p->cq0 = a->cu_seqlens_q.stride[0];
+  if (present(a->cu_seqlens_k)) { p->cu_k = reinterpret_cast<const int32_t*>(a->cu_seqlens_k.ptr); p->ck0 = a->cu_seqlens_k.stride[0]; }
+  if (present(a->seqused_k)) { p->used = reinterpret_cast<const int32_t*>(a->seqused_k.ptr); p->u0 = a->seqused_k.stride[0]; }
+  if (present(a->block_table)) {
+    p->table = reinterpret_cast<const int32_t*>(a->block_table.ptr);
+    p->bt0 = a->block_table.stride[0]; p->bt1 = a->block_table.stride[1];
+  }
+  if (present(a->leftpad_k)) { p->leftpad = reinterpret_cast<const int32_t*>(a->leftpad_k.ptr); p->lp0 = a->leftpad_k.stride[0]; }
+  if (present(a->causal_per_seq)) {
+    p->causal_b = reinterpret_cast<const uint8_t*>(a->causal_per_seq.ptr);
+    p->ca0 = a->causal_per_seq.stride[0];
+    p->dynamic = 1;
+  }
+  if (present(a->alibi_slopes)) {
+    p->alibi = reinterpret_cast<const float*>(a->alibi_slopes.ptr);
+    if (a->alibi_slopes.ndim == 1) { p->a0 = 0; p->a1 = a->alibi_slopes.stride[0]; }
+    else { p->a0 = a->alibi_slopes.stride[0]; p->a1 = a->alibi_slopes.stride[1]; }
+  }
+  if (present(a->s_aux)) { p->sinks = a->s_aux.ptr; p->sink_t = a->s_aux.dtype; p->si0 = a->s_aux.stride[0]; }
+  auto descale = [](const fa_tensor& t, const float** ptr, int64_t* s0, int64_t* s1) {
+    if (!present(t)) return;
+    *ptr = reinterpret_cast<const float*>(t.ptr);
+    *s0 = t.ndim == 2 ? t.stride[0] : 0;
+    *s1 = t.ndim == 2 ? t.stride[1] : (t.ndim == 1 ? t.stride[0] : 0);
+  };
+  descale(a->q_descale, &p->qd, &p->qd0, &p->qd1);
+  descale(a->k_descale, &p->kd, &p->kd0, &p->kd1);
+  descale(a->v_descale, &p->vd, &p->vd0, &p->vd1);
+  p->mask = a->mask_kind; p->mask_win = a->mask_window; p->clamp = a->mask_clamp;
+  if (a->mask_kind == 1) {
+    p->mr = reinterpret_cast<const int32_t*>(a->mask_aux0.ptr);
+    p->mr0 = a->mask_aux0.stride[0]; p->mr1 = a->mask_aux0.stride[1];
+  } else if (a->mask_kind == 2) {
+    p->mp = reinterpret_cast<const int32_t*>(a->mask_aux0.ptr); p->mp0 = a->mask_aux0.stride[0];
+    p->mw = reinterpret_cast<const int32_t*>(a->mask_aux1.ptr);
+  }
+  p->T = (int32_t)q.shape[0];
+  p->B = a->batch;
+  p->HQ = (int32_t)q.shape[1];
+  p->HK = (int32_t)k.shape[k.ndim - 2];
+  p->DQ = (int32_t)q.shape[2];
+  p->DV = (int32_t)v.shape[v.ndim - 1];
+  p->causal = a->causal;
+  p->win_l = a->window_left; p->win_r = a->window_right;
+  p->max_q = a->max_seqlen_q; p->max_k = a->max_seqlen_k;
+  p->scale = a->softmax_scale; p->softcap = a->softcap;
+  p->splits = 1;
+}
+
+int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
+  *plan = Plan{kRouteGeneric, 1, 0, 0, 0};
+  const bool decode = a->max_seqlen_q == 1 && !a->deterministic && !present(a->alibi_slopes) && a->mask_kind == 0;
+  if (decode) {
+    const int eff = a->window_left >= 0 ? std::min(a->max_seqlen_k, a->window_left + 1) : a->max_seqlen_k;
+    if (decode_mma_supported(p)) {
+      plan->route = kRouteDecode;
+      if (a->num_splits > 0) {
+        plan->splits = a->num_splits;
+        plan->span = std::max(1, (eff + a->num_splits - 1) / a->num_splits);
+      } else {
+        plan->splits = decode_default_splits(p, &plan->span);
+      }
+    } else {
+      // _decode.py:63-64
+      plan->splits = a->num_splits > 0 ? a->num_splits : std::max(1, std::min(32, (eff + 255) / 256));
+    }
+  } else {
+    if (!a->deterministic && a->num_splits <= 1 && prefill_sm100_supported(p)) {
+      plan->route = kRoutePrefill;
+      plan->splits = 1;
+    } else {
+      const bool vector = a->deterministic || a->max_seqlen_q == 1 || std::max(p.DQ, p.DV) > 256;
+      plan->splits = a->deterministic ? 1
+                     : a->num_splits > 0 ? a->num_splits
+                     : vector ? std::min(32, std::max(1, (a->max_seqlen_k + 255) / 256)) : 1;
+    }
+  }
+  if (plan->splits > 1) {
+    plan->part_bytes = ((size_t)plan->splits * p.T * p.HQ * p.DV * sizeof(float) + 255) / 256 * 256;
+    plan->lse_bytes = ((size_t)plan->splits * p.HQ * p.T * sizeof(float) + 255) / 256 * 256;
+  }
+  return FA_OK;
+}
+
+}  // namespace
+}  // namespace fab
+
+using namespace fab;
+
+extern "C" int fa_abi_version(void) { return FA_B200_ABI_VERSION; }
+
+extern "C" const char* fa_last_error(void) { return last_error().c_str(); }
+
+extern "C" int fa_attention_workspace_size(const fa_attention_args* a, size_t* bytes) {
+  FAB_CHECK_ARG(bytes != nullptr, "bytes must not be null");
+  *bytes = 0;
+  int rc = validate(a);
+  if (rc) return rc;
+  if (a->q.shape[0] == 0) return FA_OK;
+  AttnParams p;
+  fill_params(a, &p);
+  Plan plan;
+  rc = make_plan(a, p, &plan);
+  if (rc) return rc;
+  *bytes = plan.part_bytes + plan.lse_bytes;
+  return FA_OK;
+}
+
+extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
+  int rc = validate(a);
+  if (rc) return rc;
+  if (a->q.shape[0] == 0) return FA_OK;
+  AttnParams p;
+  fill_params(a, &p);
+  Plan plan;
+  rc = make_plan(a, p, &plan);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (plan.splits > 1) {
+    FAB_CHECK_ARG(present(a->workspace) && a->workspace.ndim >= 1 &&
+                      (size_t)a->workspace.shape[0] * elem_size(a->workspace.dtype) >= plan.part_bytes + plan.lse_bytes,
+                  "workspace smaller than fa_attention_workspace_size");
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace.ptr);
+    FAB_CHECK_ARG(((uintptr_t)ws & 15u) == 0, "workspace must be 16-byte aligned");
+    p.part = reinterpret_cast<float*>(ws);
+    p.part_lse = reinterpret_cast<float*>(ws + plan.part_bytes);
+  }
+  p.splits = plan.splits;
+  switch (plan.route) {
+    case kRouteDecode: rc = launch_decode_mma(p, plan.splits, plan.span, st); break;
+    case kRoutePrefill: rc = launch_prefill_sm100(p, st); break;
+    default: rc = launch_generic_attention(p, st); break;
+  }
+  if (rc) return rc;
+  if (plan.splits > 1) {
+    MergePartialsArgs m{};
+    m.partial = p.part; m.pdtype = FA_F32;
+    m.ps0 = (int64_t)p.T * p.HQ * p.DV; m.ps1 = (int64_t)p.HQ * p.DV; m.ps2 = p.DV; m.ps3 = 1;
+    m.lse = p.part_lse; m.ls0 = (int64_t)p.HQ * p.T; m.ls1 = p.T; m.ls2 = 1;
+    m.out = a->out.ptr; m.odtype = a->out.dtype;
+    m.os0 = a->out.stride[0]; m.os1 = a->out.stride[1]; m.os2 = a->out.stride[2];
+    m.out_lse = reinterpret_cast<float*>(a->lse.ptr);
+    m.ols0 = a->lse.stride[0]; m.ols1 = a->lse.stride[1];
+    m.S = plan.splits; m.T = p.T; m.H = p.HQ; m.D = p.DV;
+    rc = launch_merge_partials(m, st);
+  }
+  return rc;
+}

@@ -1,0 +1,417 @@
+// KV-cache bandwidth kernels: store_kvcache (slot scatter + FP8 E4M3
+// quantisation), append_kvcache and rotary position embedding.
+//
+// Semantics follow the reference flash_attn_mps 0.1.0:
+//   store   kernels/cache.metal:20-39, host _cache.py:166-184
+//   append  kernels/cache.metal:41-56, host _cache.py:198-226
+//   rotate  kernels/cache.metal:58-76, host _cache.py:229-254
+// Each thread moves one 16-byte vector of a (token, head) row when the row is
+// unit-stride and 16-byte aligned, and single elements otherwise; the grid is a
+// multiple of the SM count with a grid-stride loop.
+#include "common.cuh"
+
+namespace fab {
+namespace {
+
+struct StoreSide {
+  const void* x;
+  void* cache;
+  int64_t xs0, xs1, xs2;          // x [T,H,D]
+  int64_t cs0, cs1, cs2, cs3;     // cache [N,P,H,D]
+  int64_t capacity;               // N*P
+  const float* scale;             // FP8 only: [H] or scalar
+  int64_t scale_stride;
+  int32_t H, D, P;
+  int64_t units;                  // T*H*(D/VEC)
+};
+
+struct StoreArgs {
+  StoreSide side[2];
+  const void* slots;
+  int32_t slot_dtype;
+  int64_t slot_stride;
+};
+
+template <typename T> struct Vec16 { static constexpr int N = 16 / sizeof(T); };
+
+template <typename T, bool FP8, int VEC>
+__global__ void __launch_bounds__(256) store_kernel(StoreArgs a) {
+  const StoreSide& s = a.side[blockIdx.y];
+  if (s.x == nullptr) return;
+  const int chunks = s.D / VEC;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < s.units; u += step) {
+    const int c = (int)(u % chunks);
+    const int64_t r = u / chunks;
+    const int h = (int)(r % s.H);
+    const int64_t t = r / s.H;
+    const int64_t slot = load_index(a.slots, a.slot_dtype, t * a.slot_stride);
+    if (slot < 0 || slot >= s.capacity) continue;
+    const int64_t block = slot / s.P, off = slot - block * s.P;
+    const int64_t src = t * s.xs0 + h * s.xs1 + (int64_t)c * VEC * s.xs2;
+    const int64_t dst = block * s.cs0 + off * s.cs1 + h * s.cs2 + (int64_t)c * VEC * s.cs3;
+    const T* x = reinterpret_cast<const T*>(s.x);
+    if constexpr (!FP8) {
+      T* cache = reinterpret_cast<T*>(s.cache);
+      if constexpr (VEC * sizeof(T) == 16) {
+        *reinterpret_cast<uint4*>(cache + dst) = __ldg(reinterpret_cast<const uint4*>(x + src));
+      } else {
+        for (int i = 0; i < VEC; ++i) cache[dst + i * s.cs3] = x[src + i * s.xs2];
+      }
+    } else {
+      uint8_t* cache = reinterpret_cast<uint8_t*>(s.cache);
+      const float scale = s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+      if constexpr (VEC * sizeof(T) == 16) {
+        uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + src));
+        const T* v = reinterpret_cast<const T*>(&raw);
+        uint8_t codes[VEC];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) codes[i] = float_to_e4m3_sat(__fdiv_rn((float)v[i], scale));
+        if constexpr (VEC == 8) {
+          *reinterpret_cast<uint2*>(cache + dst) = *reinterpret_cast<const uint2*>(codes);
+        } else {
+          *reinterpret_cast<uint32_t*>(cache + dst) = *reinterpret_cast<const uint32_t*>(codes);
+        }
+      } else {
+        for (int i = 0; i < VEC; ++i)
+          cache[dst + i * s.cs3] = float_to_e4m3_sat(__fdiv_rn((float)x[src + i * s.xs2], scale));
+      }
+    }
+  }
+}
+
+bool aligned(const void* p, int64_t bytes) { return ((uintptr_t)p % bytes) == 0; }
+
+// One side (K or V) of a store call: shape checks and vector eligibility.
+int prepare_side(const fa_tensor* x, const fa_tensor* cache, const fa_tensor* scale,
+                 int64_t tokens, StoreSide* s, int* dtype, bool* fp8, bool* vec) {
+  s->x = nullptr;
+  if (!present(x)) return FA_OK;
+  FAB_CHECK_ARG(present(cache), "cache is required for each provided K/V input");
+  FAB_CHECK_ARG(x->ndim == 3 && cache->ndim == 4, "K/V must be [T,H,D] and caches [N,P,H,D]");
+  FAB_CHECK_ARG(x->shape[0] == tokens, "slot_mapping must have one slot per token");
+  FAB_CHECK_ARG(cache->shape[2] == x->shape[1] && cache->shape[3] == x->shape[2],
+                "cache must have shape [blocks, block_size, heads, dim]");
+  FAB_CHECK_ARG(is_float(x->dtype), "input dtype must be float16, bfloat16 or float32");
+  *fp8 = cache->dtype == FA_E4M3;
+  FAB_CHECK_ARG(*fp8 || cache->dtype == x->dtype, "cache dtype must match input or be float8_e4m3fn");
+  *dtype = x->dtype;
+  s->x = x->ptr;
+  s->cache = cache->ptr;
+  s->xs0 = x->stride[0]; s->xs1 = x->stride[1]; s->xs2 = x->stride[2];
+  for (int i = 0; i < 4; ++i) (&s->cs0)[i] = cache->stride[i];
+  s->H = (int32_t)x->shape[1];
+  s->D = (int32_t)x->shape[2];
+  s->P = (int32_t)cache->shape[1];
+  s->capacity = cache->shape[0] * cache->shape[1];
+  s->scale = nullptr;
+  s->scale_stride = 0;
+  if (*fp8 && present(scale)) {
+    FAB_CHECK_ARG(scale->dtype == FA_F32, "scale must be float32");
+    int64_t n = 1;
+    for (int i = 0; i < scale->ndim; ++i) n *= scale->shape[i];
+    FAB_CHECK_ARG(n == 1 || n == s->H, "scale must be scalar or have one value per KV head");
+    s->scale = reinterpret_cast<const float*>(scale->ptr);
+    s->scale_stride = n == 1 ? 0 : scale->stride[scale->ndim - 1];
+  }
+  const int esz = elem_size(x->dtype);
+  const int v = 16 / esz;
+  const int out_bytes = *fp8 ? v : 16;
+  *vec = s->D % v == 0 && s->xs2 == 1 && cache->stride[3] == 1 &&
+         aligned(x->ptr, 16) && aligned(cache->ptr, out_bytes) &&
+         (s->xs0 * esz) % 16 == 0 && (s->xs1 * esz) % 16 == 0 &&
+         (s->cs0 * (*fp8 ? 1 : esz)) % out_bytes == 0 && (s->cs1 * (*fp8 ? 1 : esz)) % out_bytes == 0 &&
+         (s->cs2 * (*fp8 ? 1 : esz)) % out_bytes == 0;
+  s->units = tokens * s->H * (int64_t)(*vec ? s->D / v : s->D);
+  return FA_OK;
+}
+
+template <typename T, bool FP8>
+void launch_store(const StoreArgs& a, bool vec, int sides, cudaStream_t stream) {
+  int64_t units = a.side[0].x ? a.side[0].units : 0;
+  if (sides > 1 && a.side[1].x) units = units > a.side[1].units ? units : a.side[1].units;
+  const int threads = 256;
+  int64_t blocks = (units + threads - 1) / threads;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  dim3 grid((unsigned)blocks, (unsigned)sides);
+  if (vec) store_kernel<T, FP8, Vec16<T>::N><<<grid, threads, 0, stream>>>(a);
+  else store_kernel<T, FP8, 1><<<grid, threads, 0, stream>>>(a);
+}
+
+int dispatch_store(const StoreArgs& a, int dtype, bool fp8, bool vec, int sides, cudaStream_t st) {
+  switch (dtype) {
+    case FA_F16: fp8 ? launch_store<__half, true>(a, vec, sides, st) : launch_store<__half, false>(a, vec, sides, st); break;
+    case FA_BF16: fp8 ? launch_store<__nv_bfloat16, true>(a, vec, sides, st) : launch_store<__nv_bfloat16, false>(a, vec, sides, st); break;
+    case FA_F32: fp8 ? launch_store<float, true>(a, vec, sides, st) : launch_store<float, false>(a, vec, sides, st); break;
+    default: return fail(FA_ERR_INVALID, "unsupported input dtype");
+  }
+  FAB_LAUNCH_CHECK("store_kvcache launch");
+  return FA_OK;
+}
+
+// ------------------------------------------------------------------ append
+struct AppendSide {
+  const void* x;
+  void* cache;
+  int64_t xs0, xs1, xs2, xs3;     // x [B,S,H,D]
+  int64_t cs0, cs1, cs2, cs3;     // cache [rows|N, capacity|P, H, D]
+  const float* scale;
+  int64_t scale_stride;
+  int32_t S, H, D;
+  int32_t xdtype, fp8;
+};
+
+struct AppendArgs {
+  AppendSide side[2];
+  const int32_t* lengths; int64_t len_stride;
+  const int32_t* batch_idx; int64_t bi_stride;
+  const int32_t* table; int64_t bt0, bt1;
+  int32_t paged, pages_per_seq, P, remap;
+  int64_t blocks, rows;
+  int64_t units;                  // B*S*H*D (max over sides)
+};
+
+__global__ void __launch_bounds__(256) append_kernel(AppendArgs a) {
+  const AppendSide& s = a.side[blockIdx.y];
+  if (s.x == nullptr) return;
+  const int64_t total = a.units;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += step) {
+    const int d = (int)(u % s.D);
+    int64_t r = u / s.D;
+    const int h = (int)(r % s.H); r /= s.H;
+    const int j = (int)(r % s.S);
+    const int64_t b = r / s.S;
+    const int64_t row = a.remap ? (int64_t)a.batch_idx[b * a.bi_stride] : b;
+    const int64_t pos = (int64_t)a.lengths[b * a.len_stride] + j;
+    const int64_t capacity = a.paged ? (int64_t)a.pages_per_seq * a.P : a.P;
+    if (row < 0 || row >= a.rows || pos < 0 || pos >= capacity) continue;
+    const int64_t block = a.paged ? (int64_t)a.table[row * a.bt0 + (pos / a.P) * a.bt1] : row;
+    const int64_t offset = a.paged ? pos % a.P : pos;
+    if (block < 0 || block >= a.blocks) continue;
+    const int64_t src = b * s.xs0 + j * s.xs1 + h * s.xs2 + d * s.xs3;
+    const int64_t dst = block * s.cs0 + offset * s.cs1 + h * s.cs2 + d * s.cs3;
+    if (s.fp8) {
+      const float scale = s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+      reinterpret_cast<uint8_t*>(s.cache)[dst] =
+          float_to_e4m3_sat(__fdiv_rn(load_float(s.x, s.xdtype, src), scale));
+    } else if (s.xdtype == FA_F32) {
+      reinterpret_cast<uint32_t*>(s.cache)[dst] = reinterpret_cast<const uint32_t*>(s.x)[src];
+    } else {
+      reinterpret_cast<uint16_t*>(s.cache)[dst] = reinterpret_cast<const uint16_t*>(s.x)[src];
+    }
+  }
+}
+
+// ------------------------------------------------------------------ rotary
+struct RotaryArgs {
+  const void* x; void* out;
+  int64_t xs0, xs1, xs2, xs3;
+  int64_t os0, os1, os2, os3;
+  const float* cos; const float* sin; int64_t cs0, cs1, ss0, ss1;
+  const int32_t* lengths; int64_t len_stride;
+  int32_t S, H, D, half, interleaved, advance, dtype;
+  int64_t units;
+};
+
+__global__ void __launch_bounds__(256) rotary_kernel(RotaryArgs a) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < a.units; u += step) {
+    const int d = (int)(u % a.D);
+    int64_t r = u / a.D;
+    const int h = (int)(r % a.H); r /= a.H;
+    const int j = (int)(r % a.S);
+    const int64_t b = r / a.S;
+    const int64_t src = b * a.xs0 + j * a.xs1 + h * a.xs2;
+    const int64_t dst = b * a.os0 + j * a.os1 + h * a.os2 + d * a.os3;
+    if (d >= 2 * a.half) {
+      if (a.dtype == FA_F32)
+        reinterpret_cast<uint32_t*>(a.out)[dst] = reinterpret_cast<const uint32_t*>(a.x)[src + d * a.xs3];
+      else
+        reinterpret_cast<uint16_t*>(a.out)[dst] = reinterpret_cast<const uint16_t*>(a.x)[src + d * a.xs3];
+      continue;
+    }
+    const int pair = a.interleaved ? d / 2 : d % a.half;
+    const bool second = a.interleaved ? (d & 1) : d >= a.half;
+    const int other = a.interleaved ? (second ? d - 1 : d + 1) : (second ? d - a.half : d + a.half);
+    const int64_t pos = (int64_t)a.lengths[b * a.len_stride] + (a.advance ? j : 0);
+    const float c = a.cos[pos * a.cs0 + pair * a.cs1], s = a.sin[pos * a.ss0 + pair * a.ss1];
+    const float x = load_float(a.x, a.dtype, src + d * a.xs3);
+    const float y = load_float(a.x, a.dtype, src + other * a.xs3);
+    // Same operation order as the reference (x*c and y*s rounded separately).
+    const float ys = __fmul_rn(y, s);
+    const float value = __fadd_rn(__fmul_rn(x, c), second ? ys : -ys);
+    store_float(a.out, a.dtype, dst, value);
+  }
+}
+
+int grid_for(int64_t units) {
+  int64_t blocks = (units + 255) / 256;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  return (int)(blocks < 1 ? 1 : blocks);
+}
+
+int prepare_append_side(const fa_tensor* x, const fa_tensor* cache, const fa_tensor* scale,
+                        int64_t batch, AppendSide* s) {
+  s->x = nullptr;
+  if (!present(x)) return FA_OK;
+  FAB_CHECK_ARG(present(cache), "cache is required for each provided K/V input");
+  FAB_CHECK_ARG(x->ndim == 4 && cache->ndim == 4, "K/V must be [B,S,H,D] and caches 4-D");
+  FAB_CHECK_ARG(x->shape[0] == batch, "K/V batch must match lengths");
+  FAB_CHECK_ARG(cache->shape[2] == x->shape[2] && cache->shape[3] == x->shape[3],
+                "cache must have shape [rows, capacity, heads, dim]");
+  FAB_CHECK_ARG(is_float(x->dtype), "input dtype must be float16, bfloat16 or float32");
+  const bool fp8 = cache->dtype == FA_E4M3;
+  FAB_CHECK_ARG(fp8 || cache->dtype == x->dtype, "cache dtype must match input or be float8_e4m3fn");
+  s->x = x->ptr; s->cache = cache->ptr;
+  for (int i = 0; i < 4; ++i) { (&s->xs0)[i] = x->stride[i]; (&s->cs0)[i] = cache->stride[i]; }
+  s->S = (int32_t)x->shape[1]; s->H = (int32_t)x->shape[2]; s->D = (int32_t)x->shape[3];
+  s->xdtype = x->dtype; s->fp8 = fp8;
+  s->scale = nullptr; s->scale_stride = 0;
+  if (fp8 && present(scale)) {
+    int64_t n = 1;
+    for (int i = 0; i < scale->ndim; ++i) n *= scale->shape[i];
+    FAB_CHECK_ARG(scale->dtype == FA_F32 && (n == 1 || n == s->H),
+                  "scale must be scalar or have one value per KV head");
+    s->scale = reinterpret_cast<const float*>(scale->ptr);
+    s->scale_stride = n == 1 ? 0 : scale->stride[scale->ndim - 1];
+  }
+  return FA_OK;
+}
+
+}  // namespace
+}  // namespace fab
+
+using namespace fab;
+
+extern "C" int fa_store_kvcache(const fa_tensor* key, const fa_tensor* value,
+                                const fa_tensor* k_cache, const fa_tensor* v_cache,
+                                const fa_tensor* slot_mapping,
+                                const fa_tensor* k_scale, const fa_tensor* v_scale,
+                                void* stream) {
+  FAB_CHECK_ARG(present(slot_mapping) && slot_mapping->ndim == 1 &&
+                    (slot_mapping->dtype == FA_I32 || slot_mapping->dtype == FA_I64),
+                "slot_mapping must be int32/int64 with one slot per token");
+  const int64_t tokens = slot_mapping->shape[0];
+  StoreArgs a{};
+  a.slots = slot_mapping->ptr;
+  a.slot_dtype = slot_mapping->dtype;
+  a.slot_stride = slot_mapping->stride[0];
+  int dt[2] = {0, 0};
+  bool fp8[2] = {false, false}, vec[2] = {false, false};
+  int rc = prepare_side(key, k_cache, k_scale, tokens, &a.side[0], &dt[0], &fp8[0], &vec[0]);
+  if (rc) return rc;
+  rc = prepare_side(value, v_cache, v_scale, tokens, &a.side[1], &dt[1], &fp8[1], &vec[1]);
+  if (rc) return rc;
+  if (tokens == 0) return FA_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool have0 = a.side[0].x != nullptr, have1 = a.side[1].x != nullptr;
+  if (have0 && have1 && dt[0] == dt[1] && fp8[0] == fp8[1] && vec[0] == vec[1]) {
+    if (a.side[0].units == 0 && a.side[1].units == 0) return FA_OK;
+    return dispatch_store(a, dt[0], fp8[0], vec[0], 2, st);
+  }
+  for (int i = 0; i < 2; ++i) {
+    if (a.side[i].x == nullptr || a.side[i].units == 0) continue;
+    StoreArgs one = a;
+    one.side[0] = a.side[i];
+    rc = dispatch_store(one, dt[i], fp8[i], vec[i], 1, st);
+    if (rc) return rc;
+  }
+  return FA_OK;
+}
+
+extern "C" int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
+                                 const fa_tensor* k_cache, const fa_tensor* v_cache,
+                                 const fa_tensor* lengths, const fa_tensor* cache_batch_idx,
+                                 const fa_tensor* block_table,
+                                 const fa_tensor* k_scale, const fa_tensor* v_scale,
+                                 void* stream) {
+  FAB_CHECK_ARG(present(lengths) && lengths->dtype == FA_I32 && lengths->ndim == 1,
+                "lengths must be int32 [B]");
+  const int64_t batch = lengths->shape[0];
+  AppendArgs a{};
+  int rc = prepare_append_side(key, k_cache, k_scale, batch, &a.side[0]);
+  if (rc) return rc;
+  rc = prepare_append_side(value, v_cache, v_scale, batch, &a.side[1]);
+  if (rc) return rc;
+  const fa_tensor* ref_cache = present(k_cache) ? k_cache : v_cache;
+  FAB_CHECK_ARG(present(ref_cache), "a cache is required");
+  a.lengths = reinterpret_cast<const int32_t*>(lengths->ptr);
+  a.len_stride = lengths->stride[0];
+  a.paged = present(block_table);
+  a.remap = !a.paged && present(cache_batch_idx);
+  if (a.remap) {
+    FAB_CHECK_ARG(cache_batch_idx->dtype == FA_I32 && cache_batch_idx->ndim == 1 &&
+                      cache_batch_idx->shape[0] == batch, "cache_batch_idx must be int32 [B]");
+    a.batch_idx = reinterpret_cast<const int32_t*>(cache_batch_idx->ptr);
+    a.bi_stride = cache_batch_idx->stride[0];
+  }
+  if (a.paged) {
+    FAB_CHECK_ARG(block_table->dtype == FA_I32 && block_table->ndim == 2,
+                  "block_table must have shape [cache_batch, blocks_per_sequence]");
+    a.table = reinterpret_cast<const int32_t*>(block_table->ptr);
+    a.bt0 = block_table->stride[0];
+    a.bt1 = block_table->stride[1];
+    a.pages_per_seq = (int32_t)block_table->shape[1];
+    a.rows = block_table->shape[0];
+  } else {
+    a.rows = ref_cache->shape[0];
+  }
+  a.P = (int32_t)ref_cache->shape[1];
+  a.blocks = ref_cache->shape[0];
+  int64_t units = 0;
+  for (int i = 0; i < 2; ++i)
+    if (a.side[i].x) {
+      const int64_t n = batch * a.side[i].S * (int64_t)a.side[i].H * a.side[i].D;
+      units = n > units ? n : units;
+    }
+  if (units == 0) return FA_OK;
+  // Each side iterates over its own element count; the shorter one exits early.
+  a.units = units;
+  AppendArgs per[2] = {a, a};
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int i = 0; i < 2; ++i) {
+    if (!a.side[i].x) continue;
+    per[i].side[0] = a.side[i];
+    per[i].units = batch * a.side[i].S * (int64_t)a.side[i].H * a.side[i].D;
+    if (per[i].units == 0) continue;
+    append_kernel<<<dim3(grid_for(per[i].units), 1), 256, 0, st>>>(per[i]);
+    FAB_LAUNCH_CHECK("append_kvcache launch");
+  }
+  return FA_OK;
+}
+
+extern "C" int fa_rotary(const fa_tensor* x, const fa_tensor* out, const fa_tensor* cos,
+                         const fa_tensor* sin, const fa_tensor* lengths, int32_t interleaved,
+                         int32_t advance, void* stream) {
+  FAB_CHECK_ARG(present(x) && present(out) && x->ndim == 4 && out->ndim == 4,
+                "Q/K must have shape [batch, tokens, heads, dim]");
+  for (int i = 0; i < 4; ++i) FAB_CHECK_ARG(x->shape[i] == out->shape[i], "out must match x");
+  FAB_CHECK_ARG(x->dtype == out->dtype && is_float(x->dtype), "x/out must share a float dtype");
+  FAB_CHECK_ARG(present(cos) && present(sin) && cos->ndim == 2 && sin->ndim == 2 &&
+                    cos->dtype == FA_F32 && sin->dtype == FA_F32 &&
+                    cos->shape[0] == sin->shape[0] && cos->shape[1] == sin->shape[1],
+                "rotary cosine/sine must be float32 [positions, rotary_dim/2]");
+  FAB_CHECK_ARG(cos->shape[1] * 2 <= x->shape[3], "rotary dimension exceeds head dimension");
+  FAB_CHECK_ARG(present(lengths) && lengths->dtype == FA_I32 && lengths->ndim == 1 &&
+                    lengths->shape[0] == x->shape[0], "lengths must be int32 [B]");
+  RotaryArgs a{};
+  a.x = x->ptr; a.out = out->ptr;
+  for (int i = 0; i < 4; ++i) { (&a.xs0)[i] = x->stride[i]; (&a.os0)[i] = out->stride[i]; }
+  a.cos = reinterpret_cast<const float*>(cos->ptr);
+  a.sin = reinterpret_cast<const float*>(sin->ptr);
+  a.cs0 = cos->stride[0]; a.cs1 = cos->stride[1]; a.ss0 = sin->stride[0]; a.ss1 = sin->stride[1];
+  a.lengths = reinterpret_cast<const int32_t*>(lengths->ptr);
+  a.len_stride = lengths->stride[0];
+  a.S = (int32_t)x->shape[1]; a.H = (int32_t)x->shape[2]; a.D = (int32_t)x->shape[3];
+  a.half = (int32_t)cos->shape[1];
+  a.interleaved = interleaved; a.advance = advance; a.dtype = x->dtype;
+  a.units = x->shape[0] * x->shape[1] * x->shape[2] * x->shape[3];
+  if (a.units == 0) return FA_OK;
+  rotary_kernel<<<grid_for(a.units), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  FAB_LAUNCH_CHECK("rotary launch");
+  return FA_OK;
+}

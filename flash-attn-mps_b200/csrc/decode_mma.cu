@@ -1,0 +1,500 @@
+// Paged / packed single-query decode on tensor cores (HBM-bound).
+//
+// Work unit: one CTA = (request b, KV head kh, block of <=16 query heads of the
+// group, KV split). The query heads of a GQA group are the N columns of the
+// MMAs, so every K/V page is read from HBM exactly once per group:
+//   S^T[tokens x heads] = K[tokens x D] * Q^T[D x heads]        (A = K tile)
+//   O^T[D x heads]     += V^T[D x tokens] * P^T[tokens x heads]  (A = V^T tile)
+// on mma.sync m16n8k16 with fp32 accumulation. Tokens as the M dimension keep
+// the padding of small groups (4 heads in an n8 tile) off the big operands.
+//   * K/V token rows are gathered through block_table with 16-byte cp.async
+//     (zero-fill outside the visible range, so NaN-poisoned tails never reach
+//     the MMAs) into an NST-stage ring of XOR-swizzled shared-memory tiles.
+//   * Each warp owns 16 tokens of a stage; the online softmax runs per head
+//     column in the log2 domain; P^T reaches the B operand of the PV MMA via
+//     movmatrix.trans, with no shared-memory round trip.
+//   * FP8 E4M3 K/V are converted in registers by the exact hardware
+//     cvt.rn.f16x2.e4m3x2; ldmatrix on byte tiles fixes a per-thread
+//     permutation of the QK reduction dimension (undone in the Q fragments)
+//     and of the output dimension (undone in the epilogue).
+//   * The warps' states are merged through shared memory; with one split the
+//     CTA writes the final output and LSE, otherwise an fp32 partial that the
+//     N-way merge kernel combines.
+// Semantics follow the reference decode_partitions
+// (flash_attn_mps/kernels/attention_decode.metal:18-149; split span and window
+// begin at 40-47, sink seeding at 54-56, softcap at 94, descales at 41-44,
+// FP8 decode at 9-16) and its dispatcher (flash_attn_mps/_decode.py:40-99).
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace fab {
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+template <bool FP8, int D, int W, int NH>
+struct Geometry {
+  static constexpr int kTile = 16 * W;                 // tokens per stage
+  static constexpr int kRowBytes = D * (FP8 ? 1 : 2);
+  static constexpr int kChunks = kRowBytes / 16;
+  static constexpr int kStageBytes = 2 * kTile * kRowBytes;
+  static constexpr int kN8 = NH / 8;                   // head tiles
+  static constexpr int kDT = D / 16;                   // 16-row output tiles per head tile
+  static_assert(kChunks >= 8 && kChunks % 8 == 0, "rows must span whole 128-byte swizzle atoms");
+};
+
+// Head-dimension index of row (g or g+8) of output tile j.
+template <bool FP8>
+__device__ __forceinline__ int out_dim(int j, int row) {
+  if constexpr (!FP8) {
+    return j * 16 + row;
+  } else {
+    // tile 2m: dims 32m + 2r (+16 for rows 8..15); tile 2m+1: the odd dims.
+    const int r = row & 7;
+    return (j >> 1) * 32 + 2 * r + (row >> 3) * 16 + (j & 1);
+  }
+}
+
+template <typename MT, bool FP8, int D, int W, int NH, int NST, bool PREC, bool QFOLD, int MINB>
+__global__ void __launch_bounds__(W * 32, MINB)
+    decode_mma_kernel(const AttnParams p, const int span, const int hblocks, const int page_shift) {
+  using G = Geometry<FP8, D, W, NH>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, qd = lane & 3;
+  const int split = blockIdx.x;
+  const int kh = blockIdx.y / hblocks, hb = blockIdx.y - kh * hblocks;
+  const int b = blockIdx.z;
+  const int token = p.cu_q[b * p.cq0];
+  if (p.cu_q[(b + 1) * p.cq0] == token) return;
+  const int group = p.HQ / p.HK;
+  const int h0 = kh * group + hb * NH;
+  const int nh = min(NH, group - hb * NH);
+  const int k_cu_begin = p.cu_k ? p.cu_k[b * p.ck0] : 0;
+  const int len = p.used ? p.used[b * p.u0] : p.cu_k[(b + 1) * p.ck0] - k_cu_begin;
+  int left = p.leftpad ? p.leftpad[b * p.lp0] : 0;
+  if (!p.paged) left += k_cu_begin;
+  const int visible_begin = p.win_l >= 0 ? max(0, len - p.win_l - 1) : 0;
+  const int begin = visible_begin + split * span;
+  const int end = min(len, begin + span);
+  const float qdesc = p.qd ? p.qd[b * p.qd0 + kh * p.qd1] : 1.f;
+  const float kdesc = p.kd ? p.kd[b * p.kd0 + kh * p.kd1] : 1.f;
+  const float vscale = p.vd ? p.vd[b * p.vd0 + kh * p.vd1] : 1.f;
+  const float scale = p.scale * qdesc * kdesc;
+  const float dot_scale = QFOLD ? 1.f : scale;  // applied to fp32 dots
+  const bool capped = p.softcap > 0.f;
+
+  // ---- Q^T fragments (B operand: k = head dim, n = query head) -------------
+  uint32_t qb[G::kN8][D / 16][2];
+#pragma unroll
+  for (int n8 = 0; n8 < G::kN8; ++n8) {
+    const int hrow = n8 * 8 + g;
+    const bool ok = hrow < nh;
+    const int64_t base = (int64_t)token * p.qs0 + (int64_t)(h0 + hrow) * p.qs1;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int khalf = 0; khalf < 2; ++khalf) {
+        const int d = FP8 ? kk * 16 + 4 * qd + 2 * khalf : kk * 16 + 8 * khalf + 2 * qd;
+        float x0 = ok ? load_float(p.q, p.qt, base + d * p.qs2) : 0.f;
+        float x1 = ok ? load_float(p.q, p.qt, base + (d + 1) * p.qs2) : 0.f;
+        if (QFOLD) { x0 *= scale; x1 *= scale; }
+        qb[n8][kk][khalf] = pack2<MT>(x0, x1);
+      }
+    }
+  }
+
+  // Per thread: head columns 2*qd, 2*qd+1 of each head tile.
+  float o[G::kN8][G::kDT][4];
+#pragma unroll
+  for (int n8 = 0; n8 < G::kN8; ++n8)
+#pragma unroll
+    for (int j = 0; j < G::kDT; ++j) o[n8][j][0] = o[n8][j][1] = o[n8][j][2] = o[n8][j][3] = 0.f;
+  float m[G::kN8][2], l[G::kN8][2];
+#pragma unroll
+  for (int n8 = 0; n8 < G::kN8; ++n8) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      m[n8][c] = -INFINITY;
+      l[n8][c] = 0.f;
+      const int hcol = n8 * 8 + 2 * qd + c;
+      if (p.sinks && split == 0 && warp == 0 && hcol < nh) {
+        m[n8][c] = load_float(p.sinks, p.sink_t, (h0 + hcol) * p.si0) * kLog2e;
+        l[n8][c] = g == 0 ? 1.f : 0.f;  // counted once across the column's lanes
+      }
+    }
+  }
+
+  // ---- K/V gather -----------------------------------------------------------
+  const int elt = FP8 ? 1 : 2;
+  const uint8_t* kglob = reinterpret_cast<const uint8_t*>(p.k) + (int64_t)kh * p.ks2 * elt;
+  const uint8_t* vglob = reinterpret_cast<const uint8_t*>(p.v) + (int64_t)kh * p.vs2 * elt;
+  const int32_t* trow = p.paged ? p.table + (int64_t)b * p.bt0 : nullptr;
+  auto load_stage = [&](int stage, int tile_start) {
+    uint8_t* ks = smem + stage * G::kStageBytes;
+    uint8_t* vs = ks + G::kTile * G::kRowBytes;
+    constexpr int kRowsPerPass = W * 32 / G::kChunks;
+    const int c = tid % G::kChunks;
+#pragma unroll
+    for (int r = tid / G::kChunks; r < G::kTile; r += kRowsPerPass) {
+      const int t = tile_start + r;
+      const bool ok = t < end;
+      int64_t koff = 0, voff = 0;
+      if (ok) {
+        const int logical = t + left;
+        if (p.paged) {
+          const int pg = page_shift >= 0 ? logical >> page_shift : logical / p.page;
+          const int in = logical - pg * p.page;
+          const int64_t blk = __ldg(trow + (int64_t)pg * p.bt1);
+          koff = blk * p.ks0 + (int64_t)in * p.ks1;
+          voff = blk * p.vs0 + (int64_t)in * p.vs1;
+        } else {
+          koff = (int64_t)logical * p.ks1;
+          voff = (int64_t)logical * p.vs1;
+        }
+      }
+      const uint32_t sw = (uint32_t)((c ^ (r & 7)) << 4);
+      cp_async_16(smem_u32(ks + r * G::kRowBytes) + sw, kglob + koff * elt + c * 16, ok ? 16 : 0);
+      cp_async_16(smem_u32(vs + r * G::kRowBytes) + sw, vglob + voff * elt + c * 16, ok ? 16 : 0);
+    }
+  };
+
+  const int n_tiles = end > begin ? (end - begin + G::kTile - 1) / G::kTile : 0;
+#pragma unroll
+  for (int s = 0; s < NST - 1; ++s) {
+    if (s < n_tiles) load_stage(s, begin + s * G::kTile);
+    cp_async_commit();
+  }
+
+  for (int it = 0; it < n_tiles; ++it) {
+    cp_async_wait<NST - 2>();
+    __syncthreads();
+    {
+      const int nxt = it + NST - 1;
+      if (nxt < n_tiles) load_stage(nxt % NST, begin + nxt * G::kTile);
+      cp_async_commit();
+    }
+    const int t0 = begin + it * G::kTile + warp * 16;
+    if (t0 >= end) continue;
+    const uint32_t kbase = smem_u32(smem + (it % NST) * G::kStageBytes);
+    const uint32_t vbase = kbase + G::kTile * G::kRowBytes;
+    const int wt0 = warp * 16;
+
+    // S^T = K Q^T over this warp's 16 tokens, as two independent MMA chains.
+    float s[G::kN8][4], s2[G::kN8][4];
+#pragma unroll
+    for (int n8 = 0; n8 < G::kN8; ++n8)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n8][e] = s2[n8][e] = 0.f;
+    {
+      const int mi = lane >> 3;
+      const int tok = wt0 + (mi & 1) * 8 + (lane & 7);
+      const uint32_t rowaddr = kbase + tok * G::kRowBytes;
+      if constexpr (!FP8) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int ch = kk * 2 + (mi >> 1);
+          uint32_t a[4];
+          ldsm_x4(rowaddr + ((ch ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int n8 = 0; n8 < G::kN8; ++n8) {
+            if (kk & 1) mma16816<MT>(s2[n8], a, qb[n8][kk][0], qb[n8][kk][1]);
+            else mma16816<MT>(s[n8], a, qb[n8][kk][0], qb[n8][kk][1]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int kc = 0; kc < D / 32; ++kc) {
+          const int ch = 2 * kc + (mi >> 1);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(rowaddr + ((ch ^ (tok & 7)) << 4), r0, r1, r2, r3);
+          uint32_t a0[4], a1[4];
+          e4m3x4_to_f16x2x2(r0, a0[0], a0[2]);
+          e4m3x4_to_f16x2x2(r1, a0[1], a0[3]);
+          e4m3x4_to_f16x2x2(r2, a1[0], a1[2]);
+          e4m3x4_to_f16x2x2(r3, a1[1], a1[3]);
+#pragma unroll
+          for (int n8 = 0; n8 < G::kN8; ++n8) {
+            mma16816<MT>(s[n8], a0, qb[n8][2 * kc][0], qb[n8][2 * kc][1]);
+            mma16816<MT>(s2[n8], a1, qb[n8][2 * kc + 1][0], qb[n8][2 * kc + 1][1]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int n8 = 0; n8 < G::kN8; ++n8)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n8][e] += s2[n8][e];
+
+    // Online softmax per head column (log2 domain). Element e of tile n8:
+    // token (e < 2 ? g : g + 8), head column 2*qd + (e & 1).
+    const bool full = t0 + 16 <= end;
+    const bool tok_lo = t0 + g < end, tok_hi = t0 + g + 8 < end;
+    bool changed = false;
+    uint32_t pb[G::kN8][2], pl[G::kN8][2];
+#pragma unroll
+    for (int n8 = 0; n8 < G::kN8; ++n8) {
+      float mx[2];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = s[n8][e];
+        if (capped) x = p.softcap * tanhf(x * dot_scale / p.softcap) * kLog2e;
+        else x *= dot_scale * kLog2e;
+        if (!full) x = (e < 2 ? tok_lo : tok_hi) ? x : -INFINITY;
+        s[n8][e] = x;
+      }
+      mx[0] = fmaxf(s[n8][0], s[n8][2]);
+      mx[1] = fmaxf(s[n8][1], s[n8][3]);
+      float nsafe[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 4));
+        mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 8));
+        mx[c] = fmaxf(mx[c], __shfl_xor_sync(0xffffffffu, mx[c], 16));
+        const float n = fmaxf(m[n8][c], mx[c]);
+        // ex2(-inf) = 0, so one guard per column keeps fully masked columns NaN-free.
+        nsafe[c] = n == -INFINITY ? 0.f : n;
+        const float f = fast_exp2(m[n8][c] - nsafe[c]);
+        changed |= f != 1.f;
+        mx[c] = f;  // reuse as the rescale factor
+        m[n8][c] = n;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n8][e] = fast_exp2(s[n8][e] - nsafe[e & 1]);
+      l[n8][0] = l[n8][0] * mx[0] + s[n8][0] + s[n8][2];
+      l[n8][1] = l[n8][1] * mx[1] + s[n8][1] + s[n8][3];
+      if (__any_sync(0xffffffffu, changed)) {
+#pragma unroll
+        for (int j = 0; j < G::kDT; ++j) {
+          o[n8][j][0] *= mx[0]; o[n8][j][1] *= mx[1];
+          o[n8][j][2] *= mx[0]; o[n8][j][3] *= mx[1];
+        }
+      }
+      // P^T as the B operand: transpose the (token, head) 8x8 blocks.
+      const uint32_t lo = pack2<MT>(s[n8][0], s[n8][1]);
+      const uint32_t hi = pack2<MT>(s[n8][2], s[n8][3]);
+      pb[n8][0] = movmatrix_t(lo);
+      pb[n8][1] = movmatrix_t(hi);
+      if constexpr (PREC) {
+        // P = hi + lo keeps ~22 bits of each probability for fp32 outputs.
+        const float2 h0f = unpack2<MT>(lo), h1f = unpack2<MT>(hi);
+        pl[n8][0] = movmatrix_t(pack2<MT>(s[n8][0] - h0f.x, s[n8][1] - h0f.y));
+        pl[n8][1] = movmatrix_t(pack2<MT>(s[n8][2] - h1f.x, s[n8][3] - h1f.y));
+      }
+    }
+
+    // O^T += V^T P^T
+    {
+      const int mi = lane >> 3;
+      const int tok = wt0 + (mi >> 1) * 8 + (lane & 7);
+      const uint32_t rowaddr = vbase + tok * G::kRowBytes;
+      if constexpr (!FP8) {
+#pragma unroll
+        for (int j = 0; j < G::kDT; ++j) {
+          const int ch = j * 2 + (mi & 1);
+          uint32_t a[4];
+          ldsm_x4_t(rowaddr + ((ch ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+#pragma unroll
+          for (int n8 = 0; n8 < G::kN8; ++n8) {
+            mma16816<MT>(o[n8][j], a, pb[n8][0], pb[n8][1]);
+            if constexpr (PREC) mma16816<MT>(o[n8][j], a, pl[n8][0], pl[n8][1]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int jg = 0; jg < D / 32; ++jg) {
+          const int ch = jg * 2 + (mi & 1);
+          uint32_t r[4];
+          ldsm_x4_t(rowaddr + ((ch ^ (tok & 7)) << 4), r[0], r[1], r[2], r[3]);
+          // Bytes (0,2) are one output dim over two tokens, (1,3) the next dim.
+          uint32_t ae[4], ao[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) e4m3x4_to_f16x2x2(__byte_perm(r[i], 0, 0x3120), ae[i], ao[i]);
+#pragma unroll
+          for (int n8 = 0; n8 < G::kN8; ++n8) {
+            mma16816<MT>(o[n8][2 * jg], ae, pb[n8][0], pb[n8][1]);
+            mma16816<MT>(o[n8][2 * jg + 1], ao, pb[n8][0], pb[n8][1]);
+            if constexpr (PREC) {
+              mma16816<MT>(o[n8][2 * jg], ae, pl[n8][0], pl[n8][1]);
+              mma16816<MT>(o[n8][2 * jg + 1], ao, pl[n8][0], pl[n8][1]);
+            }
+          }
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- merge the warps' states through shared memory -------------------------
+  float* cm = reinterpret_cast<float*>(smem);   // [W][NH]
+  float* cl = cm + W * NH;                      // [W][NH]
+  float* co = cl + W * NH;                      // [W][NH][D]
+#pragma unroll
+  for (int n8 = 0; n8 < G::kN8; ++n8) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      float x = l[n8][c];
+      x += __shfl_xor_sync(0xffffffffu, x, 4);
+      x += __shfl_xor_sync(0xffffffffu, x, 8);
+      x += __shfl_xor_sync(0xffffffffu, x, 16);
+      const int hcol = n8 * 8 + 2 * qd + c;
+      if (g == 0) {
+        cm[warp * NH + hcol] = m[n8][c];
+        cl[warp * NH + hcol] = x;
+      }
+#pragma unroll
+      for (int j = 0; j < G::kDT; ++j) {
+        co[(warp * NH + hcol) * D + out_dim<FP8>(j, g)] = o[n8][j][c];
+        co[(warp * NH + hcol) * D + out_dim<FP8>(j, g + 8)] = o[n8][j][2 + c];
+      }
+    }
+  }
+  __syncthreads();
+  constexpr int kThreadsPerHead = W * 32 / NH;
+  constexpr int kPer = D / kThreadsPerHead;
+  const int hcol = tid / kThreadsPerHead;
+  if (hcol >= nh) return;
+  float mstar = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < W; ++w) mstar = fmaxf(mstar, cm[w * NH + hcol]);
+  float wgt[W], lstar = 0.f;
+#pragma unroll
+  for (int w = 0; w < W; ++w) {
+    const float mw = cm[w * NH + hcol];
+    wgt[w] = mw == -INFINITY ? 0.f : fast_exp2(mw - mstar);
+    lstar += wgt[w] * cl[w * NH + hcol];
+  }
+  const float norm = lstar > 0.f ? vscale / lstar : 0.f;
+  const float lse = lstar > 0.f ? (mstar + log2f(lstar)) * kLn2 : -INFINITY;
+  const int h = h0 + hcol;
+  const int dbase = (tid % kThreadsPerHead) * kPer;
+  if (p.part == nullptr) {
+#pragma unroll 4
+    for (int i = 0; i < kPer; ++i) {
+      const int d = dbase + i;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) v += wgt[w] * co[(w * NH + hcol) * D + d];
+      store_float(p.out, p.ot, (int64_t)token * p.os0 + (int64_t)h * p.os1 + (int64_t)d * p.os2, v * norm);
+    }
+    if (tid % kThreadsPerHead == 0) p.lse[(int64_t)h * p.ls0 + (int64_t)token * p.ls1] = lse;
+  } else {
+    float* dst = p.part + (((int64_t)split * p.T + token) * p.HQ + h) * D;
+#pragma unroll 4
+    for (int i = 0; i < kPer; ++i) {
+      const int d = dbase + i;
+      float v = 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) v += wgt[w] * co[(w * NH + hcol) * D + d];
+      dst[d] = v * norm;
+    }
+    if (tid % kThreadsPerHead == 0) p.part_lse[((int64_t)split * p.HQ + h) * p.T + token] = lse;
+  }
+}
+
+template <bool FP8, int D, int W, int NH>
+constexpr int smem_bytes(int nst) {
+  using G = Geometry<FP8, D, W, NH>;
+  const int pipe = nst * G::kStageBytes;
+  const int merge = (2 * W * NH + W * NH * D) * 4;
+  return pipe > merge ? pipe : merge;
+}
+
+int page_shift_of(const AttnParams& p) {
+  if (!p.paged || p.page <= 0 || (p.page & (p.page - 1))) return -1;
+  int s = 0;
+  while ((1 << s) < p.page) ++s;
+  return s;
+}
+
+template <typename MT, bool FP8, int D, int NH, bool PREC, bool QFOLD>
+int launch_cfg(const AttnParams& p, int splits, int span, cudaStream_t stream) {
+  constexpr int W = FP8 ? 8 : 4;
+  constexpr int NST = 3;
+  constexpr int MINB = (FP8 && NH == 16) ? 1 : 2;
+  constexpr int smem = smem_bytes<FP8, D, W, NH>(NST);
+  auto kernel = decode_mma_kernel<MT, FP8, D, W, NH, NST, PREC, QFOLD, MINB>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(FA_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
+  const int group = p.HQ / p.HK;
+  const int hblocks = (group + NH - 1) / NH;
+  dim3 grid((unsigned)splits, (unsigned)(p.HK * hblocks), (unsigned)p.B);
+  kernel<<<grid, W * 32, smem, stream>>>(p, span, hblocks, page_shift_of(p));
+  FAB_LAUNCH_CHECK("decode launch");
+  return FA_OK;
+}
+
+template <typename MT, bool FP8, int D>
+int launch_heads(const AttnParams& p, int splits, int span, bool prec, bool qfold, cudaStream_t st) {
+  const bool wide = p.HQ / p.HK > 8;
+  if (qfold) {
+    return wide ? launch_cfg<MT, FP8, D, 16, false, true>(p, splits, span, st)
+                : launch_cfg<MT, FP8, D, 8, false, true>(p, splits, span, st);
+  }
+  if (prec) {
+    return wide ? launch_cfg<MT, FP8, D, 16, true, false>(p, splits, span, st)
+                : launch_cfg<MT, FP8, D, 8, true, false>(p, splits, span, st);
+  }
+  return wide ? launch_cfg<MT, FP8, D, 16, false, false>(p, splits, span, st)
+              : launch_cfg<MT, FP8, D, 8, false, false>(p, splits, span, st);
+}
+
+bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
+
+int tile_tokens(const AttnParams& p) { return p.kt == FA_E4M3 ? 16 * 8 : 16 * 4; }
+
+}  // namespace
+
+int decode_mma_supported(const AttnParams& p) {
+  const bool q16 = p.qt == FA_F16 || p.qt == FA_BF16;
+  if (!q16 || p.kt != p.vt) return 0;
+  const bool fp8 = p.kt == FA_E4M3;
+  if (!fp8 && p.kt != p.qt) return 0;
+  if (p.DQ != p.DV) return 0;
+  if (fp8 ? p.DQ != 128 : (p.DQ != 64 && p.DQ != 128)) return 0;
+  if (p.alibi || p.mask != 0) return 0;
+  if (p.ks3 != 1 || p.vs3 != 1) return 0;
+  const int elt = fp8 ? 1 : 2;
+  if (!aligned16(p.k) || !aligned16(p.v)) return 0;
+  const int64_t ks[3] = {p.ks0, p.ks1, p.ks2}, vs[3] = {p.vs0, p.vs1, p.vs2};
+  for (int i = p.paged ? 0 : 1; i < 3; ++i)
+    if ((ks[i] * elt) % 16 != 0 || (vs[i] * elt) % 16 != 0) return 0;
+  // bf16 queries with FP8 K/V fold the score scale into f16 queries; an fp32
+  // output asks for the reference's fp32-exact path instead.
+  if (fp8 && p.qt == FA_BF16 && p.ot == FA_F32) return 0;
+  if (p.B > 65535 || p.HK * ((p.HQ / p.HK + 15) / 16) > 65535) return 0;
+  return 1;
+}
+
+int decode_default_splits(const AttnParams& p, int* span) {
+  const int eff = p.win_l >= 0 ? min(p.max_k, p.win_l + 1) : p.max_k;
+  const int group = p.HQ / p.HK;
+  const int64_t units = (int64_t)p.B * p.HK * ((group + 15) / 16);
+  const int by_len = max(1, (eff + 255) / 256);
+  const int want = (int)((8LL * sm_count() + units - 1) / units);
+  int splits = max(want, (eff + 4095) / 4096);
+  splits = max(1, min(splits, by_len));
+  *span = (eff + splits - 1) / splits;
+  return splits;
+}
+
+int launch_decode_mma(const AttnParams& p, int splits, int span, cudaStream_t stream) {
+  const int tile = tile_tokens(p);
+  span = (span + tile - 1) / tile * tile;
+  const bool fp8 = p.kt == FA_E4M3;
+  const bool prec = p.ot == FA_F32;
+  if (fp8) {
+    const bool qfold = p.qt == FA_BF16;
+    return launch_heads<__half, true, 128>(p, splits, span, prec, qfold, stream);
+  }
+  if (p.qt == FA_BF16) {
+    return p.DQ == 64 ? launch_heads<__nv_bfloat16, false, 64>(p, splits, span, prec, false, stream)
+                      : launch_heads<__nv_bfloat16, false, 128>(p, splits, span, prec, false, stream);
+  }
+  return p.DQ == 64 ? launch_heads<__half, false, 64>(p, splits, span, prec, false, stream)
+                    : launch_heads<__half, false, 128>(p, splits, span, prec, false, stream);
+}
+
+}  // namespace fab

@@ -1,0 +1,187 @@
+/*
+ * flash_attn_b200 — C ABI of the B200 (sm_100a) FlashAttention inference kernels.
+ *
+ * This is the drop-in boundary that replaces the reference's host dispatch
+ * layer (SuperMarioYL/flash-attn-mps 0.1.0, directory flash_attn_mps/), whose
+ * Python functions compile and launch Metal shaders. Each entry point below
+ * names the reference function it replaces.
+ *
+ * Conventions
+ *  - Every tensor is an fa_tensor: a device pointer plus shape and ELEMENT
+ *    strides (not bytes), up to 4 dimensions. ptr == NULL means "absent".
+ *  - The caller owns all memory, including the split-KV workspace sized by
+ *    fa_attention_workspace_size(). The library never allocates or frees
+ *    device memory and never synchronises the host.
+ *  - Every launch is asynchronous on the caller's CUDA stream (a cudaStream_t
+ *    passed as void*; NULL = legacy default stream).
+ *  - Sequence metadata (cu_seqlens, seqused_k, block_table, slots) is read on
+ *    the device only; the host never reads tensor values.
+ *  - Return value: 0 = success, FA_ERR_INVALID = bad argument (nothing was
+ *    launched), FA_ERR_UNSUPPORTED = valid but unsupported combination,
+ *    FA_ERR_CUDA = a CUDA launch error. fa_last_error() gives the message of
+ *    the calling thread's last failure.
+ */
+#ifndef FLASH_ATTN_B200_H
+#define FLASH_ATTN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FA_B200_ABI_VERSION 1
+
+enum {
+  FA_OK = 0,
+  FA_ERR_INVALID = 1,
+  FA_ERR_UNSUPPORTED = 2,
+  FA_ERR_CUDA = 3
+};
+
+/* Element types. FA_E4M3 is float8_e4m3fn storage (one byte). */
+enum {
+  FA_DTYPE_NONE = 0,
+  FA_F16 = 1,
+  FA_BF16 = 2,
+  FA_F32 = 3,
+  FA_E4M3 = 4,
+  FA_I32 = 5,
+  FA_I64 = 6,
+  FA_BOOL = 7,
+  FA_U8 = 8
+};
+
+typedef struct fa_tensor {
+  void* ptr;
+  int32_t dtype;
+  int32_t ndim;
+  int64_t shape[4];
+  int64_t stride[4];
+} fa_tensor;
+
+/*
+ * Arguments of one attention call. Field meanings follow the reference's
+ * internal attention() (flash_attn_mps/_attention.py:170-176):
+ *   q [Tq,Hq,Dq]; k/v packed [Tk,Hkv,Dq|Dv] or paged [N,P,Hkv,Dq|Dv];
+ *   out [Tq,Hq,Dv] (f16/bf16/f32, any strides); lse [Hq,Tq] f32.
+ * Query row i of a request with Sq queries and Sk keys sits at absolute
+ * position i + Sk - Sq (lower-right causal, docs/contracts.md:32-37).
+ */
+typedef struct fa_attention_args {
+  fa_tensor q, k, v, out, lse;
+  fa_tensor cu_seqlens_q;   /* int32 [B+1] */
+  fa_tensor cu_seqlens_k;   /* int32 [B+1] or absent */
+  fa_tensor seqused_k;      /* int32 [B] or absent (exactly one of the two) */
+  fa_tensor block_table;    /* int32 [B,pages] (paged K/V) or absent */
+  fa_tensor leftpad_k;      /* int32 [B] or absent */
+  fa_tensor causal_per_seq; /* bool [B] (dynamic causal) or absent */
+  fa_tensor alibi_slopes;   /* f32 [Hq] or [B,Hq] or absent */
+  fa_tensor s_aux;          /* sinks, [Hq] f16/bf16/f32, or absent */
+  fa_tensor q_descale, k_descale, v_descale; /* f32 [B,Hkv] (zero strides allowed) */
+  fa_tensor mask_aux0, mask_aux1; /* kind 1: ranges int32 [Tq,2], cu_q int32 [B+1];
+                                     kind 2: prefix int32 [B], window int32 [1] */
+  fa_tensor workspace;      /* uint8 [bytes] from fa_attention_workspace_size */
+  int32_t batch;
+  int32_t max_seqlen_q, max_seqlen_k;
+  float softmax_scale;      /* resolved by the caller (reference default Dq^-0.5) */
+  float softcap;            /* 0 disables; applied as cap*tanh(s/cap) before masking */
+  int32_t causal;           /* static causal flag, ignored when causal_per_seq is set */
+  int32_t window_left, window_right; /* -1 = unbounded */
+  int32_t mask_kind;        /* 0 none, 1 mm-prefix, 2 rolling SWA */
+  int32_t mask_window;      /* mm-prefix sliding window (-1 none) */
+  int32_t mask_clamp;       /* mm-prefix: clamp the bidirectional range to the window */
+  int32_t num_splits;       /* 0 = library chooses; >0 exact split-KV count */
+  int32_t deterministic;    /* 1 = fixed batch-invariant reduction schedule */
+} fa_attention_args;
+
+/* Library ABI version (FA_B200_ABI_VERSION). */
+int fa_abi_version(void);
+
+/* Message of the calling thread's last failure ("" if none). */
+const char* fa_last_error(void);
+
+/*
+ * Bytes of device workspace fa_attention_fwd needs for these arguments
+ * (split-KV partial outputs and LSEs). Host-only; reads no tensor values.
+ * Replaces the partial-buffer allocation of flash_attn_mps/_attention.py:244-249
+ * and _decode.py:88-91.
+ */
+int fa_attention_workspace_size(const fa_attention_args* args, size_t* bytes);
+
+/*
+ * Attention forward: dispatch (decode / tcgen05 prefill / generic), split-KV
+ * and the LSE merge, writing out and lse.
+ * Replaces flash_attn_mps/_attention.py:170-320 (attention) together with
+ * flash_attn_mps/_decode.py:40-99 (decode_attention) which it routes to.
+ */
+int fa_attention_fwd(const fa_attention_args* args, void* stream);
+
+/*
+ * Scatter new K and V rows [T,Hkv,D] into paged caches [N,P,Hkv,D] at
+ * slot_mapping (int32/int64 [T]; slot < 0 or >= N*P is skipped). An FP8 E4M3
+ * cache stores the saturating round-to-nearest-even code of x/scale[h]
+ * (scale f32 scalar or [Hkv], absent = 1); other caches must match x's dtype
+ * and receive a bit-exact copy. Either K or V side may be absent (ptr NULL).
+ * Replaces flash_attn_mps/_cache.py:166-184 (store_kvcache) and its kernel
+ * kernels/cache.metal:20-39.
+ */
+int fa_store_kvcache(const fa_tensor* key, const fa_tensor* value,
+                     const fa_tensor* k_cache, const fa_tensor* v_cache,
+                     const fa_tensor* slot_mapping,
+                     const fa_tensor* k_scale, const fa_tensor* v_scale,
+                     void* stream);
+
+/*
+ * Append new K/V [B,Snew,Hkv,D] at positions lengths[b]+j of a continuous
+ * cache [Bcache,capacity,Hkv,D] (row cache_batch_idx[b] when given) or of a
+ * paged cache through block_table [B,pages]; out-of-range rows, positions and
+ * pages are skipped; lengths are not modified.
+ * Replaces flash_attn_mps/_cache.py:198-226 (append_kvcache), kernel
+ * kernels/cache.metal:41-56.
+ */
+int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
+                      const fa_tensor* k_cache, const fa_tensor* v_cache,
+                      const fa_tensor* lengths, const fa_tensor* cache_batch_idx,
+                      const fa_tensor* block_table,
+                      const fa_tensor* k_scale, const fa_tensor* v_scale,
+                      void* stream);
+
+/*
+ * Rotary position embedding of x [B,S,H,D] into out (same shape and dtype):
+ * position lengths[b] (+ j when advance), cos/sin f32 [positions, rot/2],
+ * interleaved or split-half pairs, dims beyond rot copied.
+ * Replaces flash_attn_mps/_cache.py:229-254 (rotary), kernel
+ * kernels/cache.metal:58-76.
+ */
+int fa_rotary(const fa_tensor* x, const fa_tensor* out,
+              const fa_tensor* cos, const fa_tensor* sin,
+              const fa_tensor* lengths, int32_t interleaved, int32_t advance,
+              void* stream);
+
+/*
+ * Stable pairwise merge of two attention states: out [T,H,D] and out_lse
+ * [H,T] (optional) may alias the left state.
+ * Replaces flash_attn_mps/_merge.py:20-41 (merge_attn_states), kernel
+ * kernels/merge.metal:9-28.
+ */
+int fa_merge_attn_states(const fa_tensor* out, const fa_tensor* left, const fa_tensor* left_lse,
+                         const fa_tensor* right, const fa_tensor* right_lse,
+                         const fa_tensor* out_lse, void* stream);
+
+/*
+ * N-way merge of split partials [S,T,H,D] (any float dtype, any strides) and
+ * LSEs [S,H,T] f32 into out [T,H,D] (f16/bf16/f32, any strides) and
+ * out_lse [H,T] f32.
+ * Replaces flash_attn_mps/_merge.py:44-57 (_merge_partials), kernels
+ * kernels/merge.metal:30-58 and kernels/attention_decode.metal:151-207.
+ */
+int fa_merge_partials(const fa_tensor* partial, const fa_tensor* partial_lse,
+                      const fa_tensor* out, const fa_tensor* out_lse, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_ATTN_B200_H */
