@@ -62,6 +62,7 @@ SIGNATURES = {
     "fa_last_error": [],
     "fa_attention_workspace_size": [_P(AttentionArgs), _P(ctypes.c_size_t)],
     "fa_attention_fwd": [_P(AttentionArgs), ctypes.c_void_p],
+    "fa_decode_fwd_noalloc": [_P(AttentionArgs), ctypes.c_void_p],
     "fa_store_kvcache": [_P(Tensor)] * 7 + [ctypes.c_void_p],
     "fa_append_kvcache": [_P(Tensor)] * 9 + [ctypes.c_void_p],
     "fa_rotary": [_P(Tensor)] * 5 + [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p],

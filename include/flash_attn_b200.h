@@ -119,6 +119,22 @@ int fa_attention_workspace_size(const fa_attention_args* args, size_t* bytes);
 int fa_attention_fwd(const fa_attention_args* args, void* stream);
 
 /*
+ * Single-query split-KV decode that allocates nothing: same arguments and
+ * results as fa_attention_fwd on its decode route (max_seqlen_q == 1, no
+ * ALiBi, no mask, not deterministic), but the split partials live in a static
+ * 32 MiB device array inside the library instead of args->workspace (which is
+ * ignored). For callers that cannot allocate device memory: FFI hosts holding
+ * only raw pointers from another allocator, processes whose device memory is
+ * pre-reserved by a pool they do not control, and decode loops that must not
+ * call cudaMalloc. Requests whose partials exceed 32 MiB fail with
+ * FA_ERR_INVALID before any launch. All calls on a device share the array:
+ * calls whose GPU work overlaps race. The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * This entry point has no counterpart in the reference.
+ */
+int fa_decode_fwd_noalloc(const fa_attention_args* args, void* stream);
+
+/*
  * Scatter new K and V rows [T,Hkv,D] into paged caches [N,P,Hkv,D] at
  * slot_mapping (int32/int64 [T]; slot < 0 or >= N*P is skipped). An FP8 E4M3
  * cache stores the saturating round-to-nearest-even code of x/scale[h]
