@@ -111,6 +111,7 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
     p->paged = 1;
   } else {
     p->ks1 = k.stride[0]; p->ks2 = k.stride[1]; p->ks3 = k.stride[2];
+    p->k_rows = k.shape[0];
     p->vs1 = v.stride[0]; p->vs2 = v.stride[1]; p->vs3 = v.stride[2];
   }
   p->out = a->out.ptr; p->ot = a->out.dtype;

@@ -42,6 +42,7 @@ struct AttnParams {
   const int32_t* mr; int64_t mr0, mr1;   // mask kind 1 ranges [T,2]
   const int32_t* mp; int64_t mp0;        // mask kind 2 prefix [B]
   const int32_t* mw;                      // mask kind 2 window [1]
+  int64_t k_rows;                        // packed K/V: rows of the K/V tensors
   int32_t T, B, HQ, HK, DQ, DV, page;
   int32_t paged, causal, dynamic, win_l, win_r;
   int32_t mask, mask_win, clamp, splits, max_q, max_k;

@@ -1,0 +1,99 @@
+"""Varlen prefill on the tcgen05 kernel (bf16/f16, head_dim 128) vs the oracle.
+
+Covers ragged lengths around the 128-row/128-key tile edges, q_len != k_len
+(lower-right causal), GQA ratios, non-causal, and the benchmark's config 2
+(32 sequences, lengths U[64, 4096], 32/8 heads) checked on sampled rows.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from flash_attn_b200 import flash_attn_varlen_func
+from helpers import assert_attention_close, assert_lse_close, cu, reference
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(device, dtype, qlens, klens, hq, hk, causal, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(sum(qlens), hq, 128, generator=g).to(dtype).to(device)
+    k = torch.randn(sum(klens), hk, 128, generator=g).to(dtype).to(device)
+    v = torch.randn(sum(klens), hk, 128, generator=g).to(dtype).to(device)
+    cq, ck = cu(qlens, device), cu(klens, device)
+    out, lse = flash_attn_varlen_func(q, k, v, cq, ck, max(qlens), max(klens), causal=causal,
+                                      return_softmax_lse=True)
+    return q, k, v, cq, ck, out, lse
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("causal", [True, False])
+def test_tile_edges(device, dtype, causal):
+    lens = [1, 7, 127, 128, 129, 255, 256, 300, 513]
+    q, k, v, cq, ck, out, lse = _run(device, dtype, lens, lens, 8, 2, causal)
+    ref, refl = reference(q, k, v, cq, ck, causal=causal)
+    assert_attention_close(out, ref, dtype)
+    assert_lse_close(lse, refl)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_query_shorter_than_keys(device, causal):
+    qlens = [1, 5, 100, 128, 200, 0, 64]
+    klens = [300, 5, 1000, 129, 700, 17, 64]
+    q, k, v, cq, ck, out, lse = _run(device, torch.bfloat16, qlens, klens, 4, 4, causal, seed=3)
+    ref, refl = reference(q, k, v, cq, ck, causal=causal)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
+
+
+def test_queries_longer_than_keys_mask_whole_rows(device):
+    # Lower-right causal: the first q_len - k_len rows see no key at all.
+    qlens, klens = [300, 130], [100, 0]
+    q, k, v, cq, ck, out, lse = _run(device, torch.float16, qlens, klens, 4, 1, True, seed=5)
+    ref, refl = reference(q, k, v, cq, ck, causal=True)
+    assert_attention_close(out, ref)
+    assert_lse_close(lse, refl)
+    assert torch.isneginf(lse[:, :200]).all() and torch.count_nonzero(out[:200]) == 0
+
+
+@pytest.mark.parametrize("hq,hk", [(32, 8), (16, 16), (8, 1)])
+def test_gqa_ratios(device, hq, hk):
+    lens = [64, 1000, 333]
+    q, k, v, cq, ck, out, lse = _run(device, torch.bfloat16, lens, lens, hq, hk, True, seed=hq)
+    ref, refl = reference(q, k, v, cq, ck, causal=True)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
+
+
+def _sample_rows_reference(q, k, v, cq, ck, b, rows, causal):
+    """Oracle on selected query rows of request b (lower-right causal positions kept)."""
+    q0, q1 = int(cq[b]), int(cq[b + 1])
+    k0, k1 = int(ck[b]), int(ck[b + 1])
+    qlen, klen = q1 - q0, k1 - k0
+    outs, lses = [], []
+    for r in rows:
+        kend = min(klen, r + 1 + klen - qlen) if causal else klen
+        qq = q[q0 + r:q0 + r + 1]
+        kk, vv = k[k0:k0 + kend], v[k0:k0 + kend]
+        o, l = reference(qq, kk, vv, torch.tensor([0, 1], dtype=torch.int32),
+                         torch.tensor([0, kend], dtype=torch.int32), causal=causal)
+        outs.append(o)
+        lses.append(l)
+    return torch.cat(outs), torch.cat(lses, dim=1)
+
+
+def test_benchmark_config2_sampled_rows(device):
+    # Config 2: 32 sequences, L ~ U[64, 4096] (seeded), 32 q / 8 kv heads, D=128, causal.
+    rng = np.random.default_rng(2)
+    lens = rng.integers(64, 4097, size=32).tolist()
+    q, k, v, cq, ck, out, lse = _run(device, torch.bfloat16, lens, lens, 32, 8, True, seed=2)
+    cqc, ckc = cq.cpu(), ck.cpu()
+    for b in (0, int(np.argmax(lens)), 17):
+        L = lens[b]
+        rows = sorted(set([0, 1, 127, 128, L // 2, L - 129, L - 2, L - 1]) & set(range(L)))
+        ref, refl = _sample_rows_reference(q, k, v, cqc, ckc, b, rows, True)
+        got = out[int(cqc[b]) + torch.tensor(rows, device=device)]
+        got_lse = lse[:, int(cqc[b]) + torch.tensor(rows, device=device)]
+        assert_attention_close(got, ref, torch.bfloat16)
+        assert_lse_close(got_lse, refl)
+    assert torch.isfinite(out).all() and torch.isfinite(lse).all()
