@@ -306,6 +306,110 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     return result
 
 
+# ------------------------------------------------- config 2 / config 3 (N=1)
+CFG2 = dict(seqs=32, lmin=64, lmax=4096, hq=32, hkv=8, d=128, seed=2)
+CFG3 = dict(batch=256, cmin=512, cmax=32768, page=16, hq=32, hkv=8, d=128, seed=3)
+
+
+def cfg2_lengths(cfg):
+    import numpy as np
+    rng = np.random.default_rng(cfg["seed"])
+    return rng.integers(cfg["lmin"], cfg["lmax"] + 1, size=cfg["seqs"]).tolist()
+
+
+def cfg2_flops(lengths, cfg, window=-1):
+    pairs = 0
+    for L in lengths:
+        if window < 0:
+            pairs += L * (L + 1) // 2
+        else:
+            w = window + 1
+            pairs += sum(min(i + 1, w) for i in range(L))
+    return cfg["hq"] * (2 * cfg["d"] + 2 * cfg["d"]) * pairs
+
+
+def time_loop(fn, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(steps):
+        fn()
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1)):
+    """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func."""
+    import torch
+    from flash_attn_b200 import flash_attn_varlen_func
+    cfg = dict(CFG2)
+    lens = cfg2_lengths(cfg)
+    total = sum(lens)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    q = torch.randn(total, cfg["hq"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
+    cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    ms = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
+                                                  softcap=softcap, window_size=window, out=out),
+                   steps, warmup)
+    flops = cfg2_flops(lens, cfg, window[0])
+    tflops = flops / (ms * 1e-3) / 1e12
+    return {"workload": "cfg2: varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
+                        + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else ""),
+            "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "TFLOP/s": tflops,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
+                         "peak_kind": f"{peak_kind} (bf16_tflops, burst)",
+                         "frac_of_sustained": tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
+
+
+def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5):
+    """Config 3: paged bf16 decode, B=256, ctx ~U[512, 32768], page 16."""
+    import numpy as np
+    import torch
+    from flash_attn_b200._attention import attention
+    cfg = dict(CFG3)
+    rng = np.random.default_rng(cfg["seed"])
+    ctx = rng.integers(cfg["cmin"], cfg["cmax"] + 1, size=cfg["batch"])
+    P = cfg["page"]
+    pages_per = (ctx + P - 1) // P
+    n_pages = int(pages_per.sum())
+    max_pages = int(pages_per.max())
+    perm = torch.from_numpy(rng.permutation(n_pages).astype(np.int32))
+    table = torch.zeros(cfg["batch"], max_pages, dtype=torch.int32)
+    off = 0
+    for b in range(cfg["batch"]):
+        table[b, :pages_per[b]] = perm[off:off + pages_per[b]]
+        off += pages_per[b]
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    kc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(cfg["batch"], cfg["hq"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    table = table.to(dev)
+    used = torch.from_numpy(ctx.astype(np.int32)).to(dev)
+    cuq = torch.arange(cfg["batch"] + 1, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    ms = time_loop(lambda: attention(q, kc, vc, cu_seqlens_q=cuq, seqused_k=used, max_seqlen_q=1,
+                                     max_seqlen_k=int(ctx.max()), block_table=table, out=out),
+                   steps, warmup)
+    nbytes = int(ctx.sum()) * cfg["hkv"] * 2 * cfg["d"] * 2 + int(pages_per.sum()) * 4 + 2 * q.numel() * 2
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del kc, vc
+    return {"workload": "cfg3: paged bf16 decode, B=256, ctx~U[512,32768], page 16, 32q/8kv, D=128",
+            "bytes_per_step": nbytes, "ms_per_step": ms, "TB/s": gbs / 1e3,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)"}}
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_fp8_decode_sample(cfg, requests=1, seed=4):
     """The oracle (reference CPU math, float64) on a bounded sample of config 4."""
@@ -374,6 +478,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode"], default="fp8_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the config-2/3 measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -393,6 +498,9 @@ def main():
                 "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"],
                 "e2e": res["e2e"], "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
                 "clocks": res["clocks"]}
+        if world == 1 and not args.no_secondary:
+            line["secondary"] = {"prefill_cfg2": run_prefill(peaks, peak_kind),
+                                 "decode_cfg3": run_bf16_decode(peaks, peak_kind)}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_block(CFG4)
         print(json.dumps(line))

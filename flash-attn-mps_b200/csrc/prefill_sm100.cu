@@ -33,23 +33,28 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128;          // query rows per tile
+constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;          // keys per tile
 constexpr int HD = 128;          // head dim
-constexpr int NS = 2;            // K/V pipeline stages
+constexpr int NSLOT = 3;         // K/V ring slots (each holds one K or one V tile)
 constexpr int kRegion = 128 * 128;            // one 128-row x 64-element box (bytes)
 constexpr int kTileBytes = 2 * kRegion;       // 128 x 128 bf16
-constexpr int kThreads = 192;
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + kTileBytes;
-constexpr int OFF_V = OFF_K + NS * kTileBytes;
-constexpr int OFF_P = OFF_V + NS * kTileBytes;
-constexpr int OFF_BAR = OFF_P + kTileBytes;
+constexpr int kThreads = 320;                 // 2 softmax warpgroups + TMA warp + MMA warp
+constexpr int OFF_QA = 0;
+constexpr int OFF_QB = OFF_QA + kTileBytes;
+constexpr int OFF_PA = OFF_QB + kTileBytes;
+constexpr int OFF_PB = OFF_PA + kTileBytes;
+constexpr int OFF_RING = OFF_PB + kTileBytes;
+constexpr int OFF_BAR = OFF_RING + NSLOT * kTileBytes;
 constexpr int kSmemBytes = OFF_BAR + 256 + 1024;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;           // S_A, S_B, O_A, O_B (128 fp32 columns each)
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays <= 2^8 between rescales
 
-enum { B_Q = 0, B_KVF = 1, B_KVE = B_KVF + NS, B_SF = B_KVE + NS, B_SE, B_PF, B_OD, B_FIN, B_COUNT };
+enum {
+  B_Q = 0, B_FULL = 1, B_EMPTY = B_FULL + NSLOT, B_SFA = B_EMPTY + NSLOT, B_SFB, B_PFA, B_PFB, B_ODA, B_ODB,
+  B_FIN, B_COUNT
+};
 
 __device__ int g_prefill_timeout;
 
@@ -59,7 +64,7 @@ struct PrefillParams {
   const int32_t* cu_q; int64_t cq0;
   const int32_t* cu_k; int64_t ck0;
   const int32_t* used; int64_t u0;
-  int32_t HQ, HK, n_qtiles, causal;
+  int32_t HQ, HK, n_pairs, causal;
   float scale_log2;
 };
 
@@ -79,6 +84,23 @@ __device__ __forceinline__ uint32_t pack_p(float a, float b) {
   }
 }
 
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// KV tiles one query tile needs: all keys up to its last visible one.
+__device__ __forceinline__ int tiles_for(int row0, int q_len, int k_len, bool causal) {
+  if (row0 >= q_len) return 0;
+  int n = (k_len + BN - 1) / BN;
+  if (causal) {
+    const int last_abs = min(row0 + BM, q_len) - 1 + k_len - q_len;
+    n = last_abs < 0 ? 0 : min(n, last_abs / BN + 1);
+  }
+  return n;
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -89,36 +111,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* gbase = smem_raw + (base - raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.z, h = blockIdx.y;
-  const int qt = p.n_qtiles - 1 - (int)blockIdx.x;  // longest causal tiles first
+  const int pair = p.n_pairs - 1 - (int)blockIdx.x;  // longest causal tiles first
   const int q_begin = p.cu_q[b * p.cq0];
   const int q_len = p.cu_q[(b + 1) * p.cq0] - q_begin;
-  if (qt * BM >= q_len) return;
+  const int row_a = pair * 2 * BM, row_b = row_a + BM;
+  if (row_a >= q_len) return;
   const int k_begin = p.cu_k ? p.cu_k[b * p.ck0] : 0;
   const int k_len = p.used ? p.used[b * p.u0] : p.cu_k[(b + 1) * p.ck0] - k_begin;
   const int kh = h / (p.HQ / p.HK);
-  int n_tiles = (k_len + BN - 1) / BN;
-  if (p.causal) {
-    const int last_abs = min(qt * BM + BM, q_len) - 1 + k_len - q_len;
-    n_tiles = last_abs < 0 ? 0 : min(n_tiles, last_abs / BN + 1);
-  }
+  const int n_a = tiles_for(row_a, q_len, k_len, p.causal);
+  const int n_b = tiles_for(row_b, q_len, k_len, p.causal);
+  const int n_all = max(n_a, n_b);
   auto bar = [&](int i) { return base + OFF_BAR + 8u * (uint32_t)i; };
   const uint32_t holder = base + OFF_BAR + 8u * B_COUNT;
   volatile uint32_t* holder_ptr = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT);
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B_Q), 1);
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(bar(B_KVF + s), 1);
-      mbar_init(bar(B_KVE + s), 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(bar(B_FULL + s), 1);
+      mbar_init(bar(B_EMPTY + s), 1);
     }
-    mbar_init(bar(B_SF), 1);
-    mbar_init(bar(B_SE), 128);
-    mbar_init(bar(B_PF), 128);
-    mbar_init(bar(B_OD), 1);
+    mbar_init(bar(B_SFA), 1);
+    mbar_init(bar(B_SFB), 1);
+    mbar_init(bar(B_PFA), 128);
+    mbar_init(bar(B_PFB), 128);
+    mbar_init(bar(B_ODA), 1);
+    mbar_init(bar(B_ODB), 1);
     mbar_init(bar(B_FIN), 1);
     mbar_fence_init();
   }
-  if (warp == 1) {
+  if (warp == 9) {
     tmem_alloc(holder, kTmemCols);
     tmem_relinquish();
   }
@@ -126,165 +149,200 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *holder_ptr;
-  const uint32_t tS = tmem, tO = tmem + 128;
 
-  if (warp == 0) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- TMA
-    int issued = 0;
-    if (n_tiles > 0) {
+    if (n_all > 0) {
+      const int items = 2 * n_all;  // K(0), V(0), K(1), V(1), ...
+      int issued = 0;
       if (lane == 0) {
         tma_prefetch_desc(&tq);
         tma_prefetch_desc(&tk);
         tma_prefetch_desc(&tv);
-        mbar_expect_tx(bar(B_Q), kTileBytes);
-        const int row = q_begin + qt * BM;
-        tma_load_3d(base + OFF_Q, &tq, bar(B_Q), 0, h, row);
-        tma_load_3d(base + OFF_Q + kRegion, &tq, bar(B_Q), 64, h, row);
+        mbar_expect_tx(bar(B_Q), 2 * kTileBytes);
+        tma_load_3d(base + OFF_QA, &tq, bar(B_Q), 0, h, q_begin + row_a);
+        tma_load_3d(base + OFF_QA + kRegion, &tq, bar(B_Q), 64, h, q_begin + row_a);
+        tma_load_3d(base + OFF_QB, &tq, bar(B_Q), 0, h, q_begin + row_b);
+        tma_load_3d(base + OFF_QB + kRegion, &tq, bar(B_Q), 64, h, q_begin + row_b);
       }
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % NS;
-        if (j >= NS && !warp_wait(bar(B_KVE + s), ((j / NS) - 1) & 1)) break;
+      for (int i = 0; i < items; ++i) {
+        const int slot = i % NSLOT;
+        if (i >= NSLOT && !warp_wait(bar(B_EMPTY + slot), ((i / NSLOT) - 1) & 1)) break;
         if (lane == 0) {
-          mbar_expect_tx(bar(B_KVF + s), 2 * kTileBytes);
-          const int row = k_begin + j * BN;
-          const uint32_t kd = base + OFF_K + s * kTileBytes, vd = base + OFF_V + s * kTileBytes;
-          tma_load_3d(kd, &tk, bar(B_KVF + s), 0, kh, row);
-          tma_load_3d(kd + kRegion, &tk, bar(B_KVF + s), 64, kh, row);
-          tma_load_3d(vd, &tv, bar(B_KVF + s), 0, kh, row);
-          tma_load_3d(vd + kRegion, &tv, bar(B_KVF + s), 64, kh, row);
+          const CUtensorMap* map = (i & 1) ? &tv : &tk;
+          const int row = k_begin + (i >> 1) * BN;
+          const uint32_t dst = base + OFF_RING + slot * kTileBytes;
+          mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
+          tma_load_3d(dst, map, bar(B_FULL + slot), 0, kh, row);
+          tma_load_3d(dst + kRegion, map, bar(B_FULL + slot), 64, kh, row);
         }
-        issued = j + 1;
+        issued = i + 1;
       }
-      // Drain: the last loads of each stage must have landed before exit.
+      // Drain: every issued load must have landed before the CTA exits.
       warp_wait(bar(B_Q), 0);
-      for (int j = max(0, issued - NS); j < issued; ++j) warp_wait(bar(B_KVF + j % NS), (j / NS) & 1);
+      for (int i = max(0, issued - NSLOT); i < issued; ++i) warp_wait(bar(B_FULL + i % NSLOT), (i / NSLOT) & 1);
     }
-  } else if (warp == 1) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA
-    if (n_tiles > 0) {
+    if (n_all > 0) {
       const uint32_t idesc_qk = f16_idesc(BM, BN, BF16 ? 1 : 0, 0);
       const uint32_t idesc_pv = f16_idesc(BM, HD, BF16 ? 1 : 0, 1);
-      auto issue_pv = [&](int jj) -> bool {
-        const int sp = jj % NS;
-        if (!warp_wait(bar(B_PF), jj & 1)) return false;
-        tc_fence_after();
-        if (lane == 0) {
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t a = sw128_desc(base + OFF_P + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(base + OFF_V + sp * kTileBytes + kk * 2048, kRegion, 1024);
-            mma_f16_ss(tO, a, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          mma_commit(bar(B_OD));
-          mma_commit(bar(B_KVE + sp));
-        }
-        __syncwarp();
-        return true;
-      };
-      bool ok = warp_wait(bar(B_Q), 0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int s = j % NS;
-        ok = warp_wait(bar(B_KVF + s), (j / NS) & 1);
-        if (ok && j > 0) ok = warp_wait(bar(B_SE), (j - 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
+      const uint32_t tSA = tmem, tSB = tmem + 128, tOA = tmem + 256, tOB = tmem + 384;
+      auto slot_addr = [&](int item) { return base + OFF_RING + (item % NSLOT) * kTileBytes; };
+      auto wait_item = [&](int item) { return warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1); };
+      auto qk = [&](uint32_t q_off, uint32_t kaddr, uint32_t d, int sfbar) {
         if (lane == 0) {
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t a = sw128_desc(base + OFF_Q + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sw128_desc(base + OFF_K + s * kTileBytes + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
-            mma_f16_ss(tS, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            const uint64_t a = sw128_desc(base + q_off + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
+            mma_f16_ss(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
           }
-          mma_commit(bar(B_SF));
+          mma_commit(bar(sfbar));
         }
         __syncwarp();
-        if (j > 0) ok = issue_pv(j - 1);
+      };
+      auto pv = [&](uint32_t p_off, uint32_t vaddr, uint32_t d, bool acc) {
+        if (lane == 0) {
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t a = sw128_desc(base + p_off + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = sw128_desc(vaddr + kk * 2048, kRegion, 1024);
+            mma_f16_ss(d, a, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          }
+        }
+        __syncwarp();
+      };
+      auto commit = [&](int barid) {
+        if (lane == 0) mma_commit(bar(barid));
+        __syncwarp();
+      };
+      bool ok = warp_wait(bar(B_Q), 0) && wait_item(0);
+      if (ok) {
+        tc_fence_after();
+        if (n_a > 0) qk(OFF_QA, slot_addr(0), tSA, B_SFA);
+        if (n_b > 0) qk(OFF_QB, slot_addr(0), tSB, B_SFB);
+        commit(B_EMPTY + 0);
       }
-      if (ok) issue_pv(n_tiles - 1);
+      for (int j = 0; ok && j < n_all; ++j) {
+        const int iv = 2 * j + 1, ik = 2 * j + 2;
+        if (!(ok = wait_item(iv))) break;
+        if (j < n_a) {
+          if (!(ok = warp_wait(bar(B_PFA), j & 1))) break;
+          tc_fence_after();
+          pv(OFF_PA, slot_addr(iv), tOA, j > 0);
+          if (j == n_a - 1) commit(B_ODA);
+        }
+        const bool next = j + 1 < n_all;
+        if (next && !(ok = wait_item(ik))) break;
+        tc_fence_after();
+        if (j + 1 < n_a) qk(OFF_QA, slot_addr(ik), tSA, B_SFA);
+        if (j < n_b) {
+          if (!(ok = warp_wait(bar(B_PFB), j & 1))) break;
+          tc_fence_after();
+          pv(OFF_PB, slot_addr(iv), tOB, j > 0);
+          if (j == n_b - 1) commit(B_ODB);
+        }
+        commit(B_EMPTY + iv % NSLOT);
+        if (j + 1 < n_b) qk(OFF_QB, slot_addr(ik), tSB, B_SFB);
+        if (next) commit(B_EMPTY + ik % NSLOT);
+      }
       // All MMAs of this CTA must be complete before TMEM is released.
-      if (lane == 0) mma_commit(bar(B_FIN));
-      __syncwarp();
+      commit(B_FIN);
       warp_wait(bar(B_FIN), 0);
     }
   } else {
     // ------------------------------------------------------------ softmax
+    const bool is_b = warp >= 4;
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-    const int q_row = qt * BM + row;
+    const uint32_t tS = tmem + (is_b ? 128 : 0) + lane_off;
+    const uint32_t tO = tmem + (is_b ? 384 : 256) + lane_off;
+    const int n_x = is_b ? n_b : n_a;
+    const int q_row = (is_b ? row_b : row_a) + row;
     const int q_abs = q_row + k_len - q_len;
-    float m_run = -INFINITY, l_run = 0.f;
+    const int sf = is_b ? B_SFB : B_SFA, pf = is_b ? B_PFB : B_PFA, od = is_b ? B_ODB : B_ODA;
+    uint8_t* prow = gbase + (is_b ? OFF_PB : OFF_PA) + row * 128;
+    const float sl2 = p.scale_log2;
+    float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
     bool ok = true;
-    uint8_t* prow0 = gbase + OFF_P + row * 128;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!(ok = warp_wait(bar(B_SF), j & 1))) break;
+    for (int j = 0; j < n_x; ++j) {
+      if (!(ok = warp_wait(bar(sf), j & 1))) break;
       tc_fence_after();
-      float s[BN];
+      const int key0 = j * BN;
+      const bool need_mask = key0 + BN > k_len || (p.causal && key0 + BN - 1 > q_abs);
+      const int limit = (p.causal ? min(k_len - 1, q_abs) : k_len - 1) - key0;  // last visible column
+      // Pass 1: row max of the raw scores.
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tS + lane_off + c * 32, r);
+        tmem_ld32(tS + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(bar(B_SE));
-      const int key0 = j * BN;
-      const bool need_mask = key0 + BN > k_len || (p.causal && key0 + BN - 1 > q_abs);
-      const int limit = p.causal ? min(k_len - 1, q_abs) : k_len - 1;  // last visible key
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        float x = s[i] * p.scale_log2;
-        if (need_mask && key0 + i > limit) x = -INFINITY;
-        s[i] = x;
-        mx = fmaxf(mx, x);
-      }
-      const float m_new = fmaxf(m_run, mx);
-      const float m_safe = m_new == -INFINITY ? 0.f : m_new;
-      const float factor = exp2f(m_run - m_safe);
-      if (j > 0) {
-        if (!(ok = warp_wait(bar(B_OD), (j - 1) & 1))) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, factor != 1.f)) {
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tO + lane_off + c * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tmem_st32(tO + lane_off + c * 32, r);
-          }
-          tmem_wait_st();
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(r[i]);
+          mx = (need_mask && c * 32 + i > limit) ? mx : fmaxf(mx, x);
         }
+      }
+      const float m_tile = mx * sl2;  // scale > 0: max commutes with scaling
+      float factor = 1.f;
+      if (m_tile > m_run + kRescaleThreshold || (m_run == -INFINITY && m_tile != -INFINITY)) {
+        factor = m_run == -INFINITY ? 0.f : ex2(m_run - m_tile);
+        m_run = m_tile;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+          tmem_st32(tO + c * 32, r);
+        }
+        tmem_wait_st();
       }
       l_run *= factor;
-      m_run = m_new;
+      const float msub = m_run == -INFINITY ? 0.f : m_run;
+      // Pass 2: P = 2^(s*scale_log2 - m) written to the swizzled P tile.
       float lsum = 0.f;
 #pragma unroll
-      for (int chunk = 0; chunk < BN / 8; ++chunk) {
-        uint32_t w[4];
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tS + c * 32, r);
+        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float p0 = exp2f(s[chunk * 8 + 2 * i] - m_safe);
-          const float p1 = exp2f(s[chunk * 8 + 2 * i + 1] - m_safe);
-          lsum += p0 + p1;
-          w[i] = pack_p<BF16>(p0, p1);
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int col0 = c * 32 + q4 * 8 + 2 * i;
+            float p0 = ex2(fmaf(__uint_as_float(r[q4 * 8 + 2 * i]), sl2, -msub));
+            float p1 = ex2(fmaf(__uint_as_float(r[q4 * 8 + 2 * i + 1]), sl2, -msub));
+            if (need_mask) {
+              p0 = col0 > limit ? 0.f : p0;
+              p1 = col0 + 1 > limit ? 0.f : p1;
+            }
+            lsum += p0 + p1;
+            w[i] = pack_p<BF16>(p0, p1);
+          }
+          const int chunk = c * 4 + q4, region = chunk >> 3, cc = chunk & 7;
+          *reinterpret_cast<uint4*>(prow + region * kRegion + ((cc ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
-        const int region = chunk >> 3, cc = chunk & 7;
-        *reinterpret_cast<uint4*>(prow0 + region * kRegion + ((cc ^ (row & 7)) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
       }
       l_run += lsum;
       if (key0 + BN > k_len) {
         // Keys past the sequence in the last tile: zero their V rows so that a
         // non-finite neighbour value can never meet a zero probability.
-        const int s = j % NS;
-        if (!(ok = warp_wait(bar(B_KVF + s), (j / NS) & 1))) break;
+        const int item = 2 * j + 1;
+        if (!(ok = warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1))) break;
+        // Each warpgroup that consumes this tile zeroes the rows itself before
+        // releasing its P (identical zero stores, no cross-group barrier).
         if (key0 + row >= k_len) {
-          uint8_t* vrow = gbase + OFF_V + s * kTileBytes + row * 128;
+          uint8_t* vrow = gbase + OFF_RING + (item % NSLOT) * kTileBytes + row * 128;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
@@ -294,23 +352,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar(B_PF));
+      mbar_arrive(bar(pf));
     }
-    if (ok && n_tiles > 0) {
-      ok = warp_wait(bar(B_OD), (n_tiles - 1) & 1);
+    if (ok && n_x > 0) {
+      ok = warp_wait(bar(od), 0);
       tc_fence_after();
     }
     // ------------------------------------------------------------ epilogue
     const bool row_ok = q_row < q_len;
     const int64_t t = (int64_t)q_begin + q_row;
-    const bool have = ok && n_tiles > 0 && l_run > 0.f;
+    const bool have = ok && n_x > 0 && l_run > 0.f;
     const float inv = have ? 1.f / l_run : 0.f;
     uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + (t * p.os0 + (int64_t)h * p.os1) * 2;
 #pragma unroll
     for (int c = 0; c < HD / 32; ++c) {
       uint32_t r[32];
-      if (ok && n_tiles > 0) {
-        tmem_ld32(tO + lane_off + c * 32, r);
+      if (ok && n_x > 0) {
+        tmem_ld32(tO + c * 32, r);
         tmem_wait_ld();
       }
       if (row_ok) {
@@ -331,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -404,13 +462,13 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.cu_k = p.cu_k; pp.ck0 = p.ck0;
   pp.used = p.used; pp.u0 = p.u0;
   pp.HQ = p.HQ; pp.HK = p.HK;
-  pp.n_qtiles = (p.max_q + BM - 1) / BM;
+  pp.n_pairs = (p.max_q + 2 * BM - 1) / (2 * BM);
   pp.causal = p.causal;
   pp.scale_log2 = p.scale * 1.4426950408889634f;
   auto kernel = p.qt == FA_BF16 ? prefill_sm100_kernel<true> : prefill_sm100_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
-  dim3 grid((unsigned)pp.n_qtiles, (unsigned)p.HQ, (unsigned)p.B);
+  dim3 grid((unsigned)pp.n_pairs, (unsigned)p.HQ, (unsigned)p.B);
   kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, pp);
   FAB_LAUNCH_CHECK("prefill launch");
   return FA_OK;
