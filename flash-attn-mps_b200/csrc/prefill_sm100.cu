@@ -273,19 +273,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key0 = j * BN;
       const bool need_mask = key0 + BN > k_len || (p.causal && key0 + BN - 1 > q_abs);
       const int limit = (p.causal ? min(k_len - 1, q_abs) : k_len - 1) - key0;  // last visible column
-      // Pass 1: row max of the raw scores.
-      float mx = -INFINITY;
+      // Pass 1: row max, 64 columns (two TMEM loads in flight) at a time, as 8
+      // independent chains (fp max is exact in any order).
+      float mx8[8];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
+      for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = -INFINITY;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t r[64];
+        tmem_ld32_at<0>(tS + hh * 64, r);
+        tmem_ld32_at<32>(tS + hh * 64 + 32, r);
         tmem_wait_ld();
+        if (need_mask) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(r[i]);
-          mx = (need_mask && c * 32 + i > limit) ? mx : fmaxf(mx, x);
+          for (int i = 0; i < 64; ++i)
+            if (hh * 64 + i > limit) r[i] = __float_as_uint(-INFINITY);
         }
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[i]));
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_tile = mx * sl2;  // scale > 0: max commutes with scaling
       float factor = 1.f;
       if (m_tile > m_run + kRescaleThreshold || (m_run == -INFINITY && m_tile != -INFINITY)) {
@@ -295,44 +303,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          tmem_st32(tO + c * 32, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st32(tO + c * 32, o);
         }
         tmem_wait_st();
       }
       l_run *= factor;
       const float msub = m_run == -INFINITY ? 0.f : m_run;
-      // Pass 2: P = 2^(s*scale_log2 - m) written to the swizzled P tile.
-      float lsum = 0.f;
+      // Pass 2: P = 2^(s*scale_log2 - m), masked columns -> 0, written to the
+      // swizzled P tile; the row sum runs as 8 independent chains.
+      float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS + c * 32, r);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t r[64];
+        tmem_ld32_at<0>(tS + hh * 64, r);
+        tmem_ld32_at<32>(tS + hh * 64 + 32, r);
         tmem_wait_ld();
+        if (need_mask) {
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
+          for (int i = 0; i < 64; ++i)
+            if (hh * 64 + i > limit) r[i] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int col0 = c * 32 + q4 * 8 + 2 * i;
-            float p0 = ex2(fmaf(__uint_as_float(r[q4 * 8 + 2 * i]), sl2, -msub));
-            float p1 = ex2(fmaf(__uint_as_float(r[q4 * 8 + 2 * i + 1]), sl2, -msub));
-            if (need_mask) {
-              p0 = col0 > limit ? 0.f : p0;
-              p1 = col0 + 1 > limit ? 0.f : p1;
-            }
-            lsum += p0 + p1;
+            const float p0 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i]), sl2, -msub));
+            const float p1 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i + 1]), sl2, -msub));
+            ls8[2 * i] += p0;
+            ls8[2 * i + 1] += p1;
             w[i] = pack_p<BF16>(p0, p1);
           }
-          const int chunk = c * 4 + q4, region = chunk >> 3, cc = chunk & 7;
+          const int chunk = hh * 8 + c8, region = chunk >> 3, cc = chunk & 7;
           *reinterpret_cast<uint4*>(prow + region * kRegion + ((cc ^ (row & 7)) << 4)) =
               make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+      const float lsum = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
       l_run += lsum;
       if (key0 + BN > k_len) {
         // Keys past the sequence in the last tile: zero their V rows so that a
