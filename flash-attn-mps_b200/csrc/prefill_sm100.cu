@@ -64,8 +64,13 @@ struct PrefillParams {
   const int32_t* cu_q; int64_t cq0;
   const int32_t* cu_k; int64_t ck0;
   const int32_t* used; int64_t u0;
-  int32_t HQ, HK, n_pairs, causal;
-  float scale_log2;
+  const uint8_t* causal_b; int64_t ca0;     // dynamic per-request causal flags
+  const void* sinks; int32_t sink_t; int64_t si0;
+  const float* qd; int64_t qd0, qd1;
+  const float* kd; int64_t kd0, kd1;
+  const float* vd; int64_t vd0, vd1;
+  int32_t HQ, HK, n_pairs, causal, win_l, win_r;
+  float scale, softcap;
 };
 
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
@@ -90,18 +95,31 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// KV tiles one query tile needs: all keys up to its last visible one.
-__device__ __forceinline__ int tiles_for(int row0, int q_len, int k_len, bool causal) {
-  if (row0 >= q_len) return 0;
-  int n = (k_len + BN - 1) / BN;
-  if (causal) {
-    const int last_abs = min(row0 + BM, q_len) - 1 + k_len - q_len;
-    n = last_abs < 0 ? 0 : min(n, last_abs / BN + 1);
-  }
-  return n;
+// Visible key range [lo, hi] of the query at absolute position q_abs
+// (lower-right causal, local window), clipped to [0, k_len).
+struct KeyRange { int lo, hi; };
+__device__ __forceinline__ KeyRange key_range(int q_abs, int k_len, bool causal, int win_l, int win_r) {
+  int lo = win_l >= 0 ? max(0, q_abs - win_l) : 0;
+  int hi = k_len - 1;
+  if (causal) hi = min(hi, q_abs);
+  if (win_r >= 0) hi = min(hi, q_abs + win_r);
+  return {lo, hi};
 }
 
-template <bool BF16>
+// KV tiles [first, last) that a 128-row query tile starting at row0 touches.
+__device__ __forceinline__ void tile_range(int row0, int q_len, int k_len, bool causal, int win_l, int win_r,
+                                           int* first, int* last) {
+  *first = *last = 0;
+  if (row0 >= q_len || k_len <= 0) return;
+  const int off = k_len - q_len;
+  const KeyRange a = key_range(row0 + off, k_len, causal, win_l, win_r);
+  const KeyRange z = key_range(min(row0 + BM, q_len) - 1 + off, k_len, causal, win_l, win_r);
+  if (z.hi < a.lo || z.hi < 0) return;
+  *first = a.lo / BN;
+  *last = z.hi / BN + 1;
+}
+
+template <bool BF16, bool SOFTCAP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
@@ -119,9 +137,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k_begin = p.cu_k ? p.cu_k[b * p.ck0] : 0;
   const int k_len = p.used ? p.used[b * p.u0] : p.cu_k[(b + 1) * p.ck0] - k_begin;
   const int kh = h / (p.HQ / p.HK);
-  const int n_a = tiles_for(row_a, q_len, k_len, p.causal);
-  const int n_b = tiles_for(row_b, q_len, k_len, p.causal);
-  const int n_all = max(n_a, n_b);
+  const bool causal = p.causal_b ? p.causal_b[b * p.ca0] != 0 : p.causal != 0;
+  int a0, a1, b0, b1;
+  tile_range(row_a, q_len, k_len, causal, p.win_l, p.win_r, &a0, &a1);
+  tile_range(row_b, q_len, k_len, causal, p.win_l, p.win_r, &b0, &b1);
+  const int n_a = a1 - a0, n_b = b1 - b0;
+  // KV tiles [j_first, j_last) cover both query tiles; item i = 2*(j - j_first) (+1 for V).
+  const int j_first = n_a > 0 ? (n_b > 0 ? min(a0, b0) : a0) : b0;
+  const int j_last = max(n_a > 0 ? a1 : 0, n_b > 0 ? b1 : 0);
+  const int n_all = (n_a > 0 || n_b > 0) ? j_last - j_first : 0;
   auto bar = [&](int i) { return base + OFF_BAR + 8u * (uint32_t)i; };
   const uint32_t holder = base + OFF_BAR + 8u * B_COUNT;
   volatile uint32_t* holder_ptr = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT);
@@ -170,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i >= NSLOT && !warp_wait(bar(B_EMPTY + slot), ((i / NSLOT) - 1) & 1)) break;
         if (lane == 0) {
           const CUtensorMap* map = (i & 1) ? &tv : &tk;
-          const int row = k_begin + (i >> 1) * BN;
+          const int row = k_begin + (j_first + (i >> 1)) * BN;
           const uint32_t dst = base + OFF_RING + slot * kTileBytes;
           mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
           tma_load_3d(dst, map, bar(B_FULL + slot), 0, kh, row);
@@ -217,34 +241,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mma_commit(bar(barid));
         __syncwarp();
       };
+      auto act_a = [&](int j) { return j >= a0 && j < a1; };
+      auto act_b = [&](int j) { return j >= b0 && j < b1; };
       bool ok = warp_wait(bar(B_Q), 0) && wait_item(0);
       if (ok) {
         tc_fence_after();
-        if (n_a > 0) qk(OFF_QA, slot_addr(0), tSA, B_SFA);
-        if (n_b > 0) qk(OFF_QB, slot_addr(0), tSB, B_SFB);
+        if (act_a(j_first)) qk(OFF_QA, slot_addr(0), tSA, B_SFA);
+        if (act_b(j_first)) qk(OFF_QB, slot_addr(0), tSB, B_SFB);
         commit(B_EMPTY + 0);
       }
-      for (int j = 0; ok && j < n_all; ++j) {
-        const int iv = 2 * j + 1, ik = 2 * j + 2;
+      for (int t = 0; ok && t < n_all; ++t) {
+        const int j = j_first + t;
+        const int iv = 2 * t + 1, ik = 2 * t + 2;
         if (!(ok = wait_item(iv))) break;
-        if (j < n_a) {
-          if (!(ok = warp_wait(bar(B_PFA), j & 1))) break;
+        if (act_a(j)) {
+          if (!(ok = warp_wait(bar(B_PFA), (j - a0) & 1))) break;
           tc_fence_after();
-          pv(OFF_PA, slot_addr(iv), tOA, j > 0);
-          if (j == n_a - 1) commit(B_ODA);
+          pv(OFF_PA, slot_addr(iv), tOA, j > a0);
+          if (j == a1 - 1) commit(B_ODA);
         }
-        const bool next = j + 1 < n_all;
+        const bool next = t + 1 < n_all;
         if (next && !(ok = wait_item(ik))) break;
         tc_fence_after();
-        if (j + 1 < n_a) qk(OFF_QA, slot_addr(ik), tSA, B_SFA);
-        if (j < n_b) {
-          if (!(ok = warp_wait(bar(B_PFB), j & 1))) break;
+        if (next && act_a(j + 1)) qk(OFF_QA, slot_addr(ik), tSA, B_SFA);
+        if (act_b(j)) {
+          if (!(ok = warp_wait(bar(B_PFB), (j - b0) & 1))) break;
           tc_fence_after();
-          pv(OFF_PB, slot_addr(iv), tOB, j > 0);
-          if (j == n_b - 1) commit(B_ODB);
+          pv(OFF_PB, slot_addr(iv), tOB, j > b0);
+          if (j == b1 - 1) commit(B_ODB);
         }
         commit(B_EMPTY + iv % NSLOT);
-        if (j + 1 < n_b) qk(OFF_QB, slot_addr(ik), tSB, B_SFB);
+        if (next && act_b(j + 1)) qk(OFF_QB, slot_addr(ik), tSB, B_SFB);
         if (next) commit(B_EMPTY + ik % NSLOT);
       }
       // All MMAs of this CTA must be complete before TMEM is released.
@@ -259,20 +286,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
     const uint32_t tS = tmem + (is_b ? 128 : 0) + lane_off;
     const uint32_t tO = tmem + (is_b ? 384 : 256) + lane_off;
-    const int n_x = is_b ? n_b : n_a;
+    const int x0 = is_b ? b0 : a0, n_x = is_b ? n_b : n_a;
     const int q_row = (is_b ? row_b : row_a) + row;
     const int q_abs = q_row + k_len - q_len;
+    const KeyRange vis = key_range(q_abs, k_len, causal, p.win_l, p.win_r);
     const int sf = is_b ? B_SFB : B_SFA, pf = is_b ? B_PFB : B_PFA, od = is_b ? B_ODB : B_ODA;
     uint8_t* prow = gbase + (is_b ? OFF_PB : OFF_PA) + row * 128;
-    const float sl2 = p.scale_log2;
-    float m_run = -INFINITY, l_run = 0.f;  // m_run in scaled log2 units
+    const float qk_scale = p.scale * (p.qd ? p.qd[b * p.qd0 + kh * p.qd1] : 1.f) *
+                           (p.kd ? p.kd[b * p.kd0 + kh * p.kd1] : 1.f);
+    const float vscale = p.vd ? p.vd[b * p.vd0 + kh * p.vd1] : 1.f;
+    const float sl2 = qk_scale * 1.4426950408889634f;       // raw score -> log2 units
+    const float cap_l2 = p.softcap * 1.4426950408889634f;    // softcap: cap*log2e*tanh(s*scale/cap)
+    const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
+    // Running max in log2 units; a sink acts as one extra logit with zero value.
+    float m_run = -INFINITY, l_run = 0.f;
+    if (p.sinks) {
+      m_run = load_float(p.sinks, p.sink_t, h * p.si0) * 1.4426950408889634f;
+      l_run = 1.f;
+    }
     bool ok = true;
-    for (int j = 0; j < n_x; ++j) {
-      if (!(ok = warp_wait(bar(sf), j & 1))) break;
+    for (int jj = 0; jj < n_x; ++jj) {
+      const int j = x0 + jj;
+      if (!(ok = warp_wait(bar(sf), jj & 1))) break;
       tc_fence_after();
       const int key0 = j * BN;
-      const bool need_mask = key0 + BN > k_len || (p.causal && key0 + BN - 1 > q_abs);
-      const int limit = (p.causal ? min(k_len - 1, q_abs) : k_len - 1) - key0;  // last visible column
+      const int c_lo = vis.lo - key0, c_hi = vis.hi - key0;  // visible columns of this tile
+      const bool need_mask = c_lo > 0 || c_hi < BN - 1;
       // Pass 1: row max, 64 columns (two TMEM loads in flight) at a time, as 8
       // independent chains (fp max is exact in any order).
       float mx8[8];
@@ -287,20 +326,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            if (hh * 64 + i > limit) r[i] = __float_as_uint(-INFINITY);
+            if (hh * 64 + i < c_lo || hh * 64 + i > c_hi) r[i] = __float_as_uint(-INFINITY);
         }
 #pragma unroll
         for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[i]));
       }
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float m_tile = mx * sl2;  // scale > 0: max commutes with scaling
+      // scale > 0 and tanh is increasing: the max commutes with both.
+      const float m_tile = SOFTCAP ? (mx == -INFINITY ? -INFINITY : cap_l2 * tanhf(mx * cap_in)) : mx * sl2;
       float factor = 1.f;
       if (m_tile > m_run + kRescaleThreshold || (m_run == -INFINITY && m_tile != -INFINITY)) {
         factor = m_run == -INFINITY ? 0.f : ex2(m_run - m_tile);
         m_run = m_tile;
       }
-      if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+      if (jj > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           uint32_t o[32];
@@ -326,15 +366,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            if (hh * 64 + i > limit) r[i] = __float_as_uint(-INFINITY);
+            if (hh * 64 + i < c_lo || hh * 64 + i > c_hi) r[i] = __float_as_uint(-INFINITY);
         }
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t w[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float p0 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i]), sl2, -msub));
-            const float p1 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i + 1]), sl2, -msub));
+            float p0, p1;
+            if constexpr (SOFTCAP) {
+              const float s0 = __uint_as_float(r[c8 * 8 + 2 * i]), s1 = __uint_as_float(r[c8 * 8 + 2 * i + 1]);
+              p0 = s0 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanhf(s0 * cap_in), -msub));
+              p1 = s1 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanhf(s1 * cap_in), -msub));
+            } else {
+              p0 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i]), sl2, -msub));
+              p1 = ex2(fmaf(__uint_as_float(r[c8 * 8 + 2 * i + 1]), sl2, -msub));
+            }
             ls8[2 * i] += p0;
             ls8[2 * i + 1] += p1;
             w[i] = pack_p<BF16>(p0, p1);
@@ -349,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (key0 + BN > k_len) {
         // Keys past the sequence in the last tile: zero their V rows so that a
         // non-finite neighbour value can never meet a zero probability.
-        const int item = 2 * j + 1;
+        const int item = 2 * (j - j_first) + 1;
         if (!(ok = warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1))) break;
         // Each warpgroup that consumes this tile zeroes the rows itself before
         // releasing its P (identical zero stores, no cross-group barrier).
@@ -374,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool row_ok = q_row < q_len;
     const int64_t t = (int64_t)q_begin + q_row;
     const bool have = ok && n_x > 0 && l_run > 0.f;
-    const float inv = have ? 1.f / l_run : 0.f;
+    const float inv = have ? vscale / l_run : 0.f;
     uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + (t * p.os0 + (int64_t)h * p.os1) * 2;
 #pragma unroll
     for (int c = 0; c < HD / 32; ++c) {
@@ -397,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (row_ok) p.lse[(int64_t)h * p.ls0 + t * p.ls1] = have ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+    if (row_ok) p.lse[(int64_t)h * p.ls0 + t * p.ls1] = ok && l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
@@ -445,9 +492,8 @@ bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 int prefill_sm100_supported(const AttnParams& p) {
   if (!(p.qt == FA_BF16 || p.qt == FA_F16) || p.kt != p.qt || p.vt != p.qt || p.ot != p.qt) return 0;
   if (p.DQ != HD || p.DV != HD || p.paged) return 0;
-  if (p.win_l >= 0 || p.win_r >= 0 || p.alibi || p.sinks || p.qd || p.kd || p.vd || p.mask || p.leftpad ||
-      p.dynamic || p.softcap > 0.f)
-    return 0;
+  if (p.alibi || p.mask || p.leftpad) return 0;
+  if (p.sinks && !(p.sink_t == FA_F32 || p.sink_t == FA_F16 || p.sink_t == FA_BF16)) return 0;
   if (p.qs2 != 1 || p.ks3 != 1 || p.vs3 != 1 || p.os2 != 1) return 0;
   if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !al16(p.out)) return 0;
   const int64_t s[8] = {p.qs0, p.qs1, p.ks1, p.ks2, p.vs1, p.vs2, p.os0, p.os1};
@@ -476,8 +522,17 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.HQ = p.HQ; pp.HK = p.HK;
   pp.n_pairs = (p.max_q + 2 * BM - 1) / (2 * BM);
   pp.causal = p.causal;
-  pp.scale_log2 = p.scale * 1.4426950408889634f;
-  auto kernel = p.qt == FA_BF16 ? prefill_sm100_kernel<true> : prefill_sm100_kernel<false>;
+  pp.causal_b = p.dynamic ? p.causal_b : nullptr; pp.ca0 = p.ca0;
+  pp.sinks = p.sinks; pp.sink_t = p.sink_t; pp.si0 = p.si0;
+  pp.qd = p.qd; pp.qd0 = p.qd0; pp.qd1 = p.qd1;
+  pp.kd = p.kd; pp.kd0 = p.kd0; pp.kd1 = p.kd1;
+  pp.vd = p.vd; pp.vd0 = p.vd0; pp.vd1 = p.vd1;
+  pp.win_l = p.win_l; pp.win_r = p.win_r;
+  pp.scale = p.scale;
+  pp.softcap = p.softcap;
+  const bool cap = p.softcap > 0.f;
+  auto kernel = p.qt == FA_BF16 ? (cap ? prefill_sm100_kernel<true, true> : prefill_sm100_kernel<true, false>)
+                                : (cap ? prefill_sm100_kernel<false, true> : prefill_sm100_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)pp.n_pairs, (unsigned)p.HQ, (unsigned)p.B);

@@ -97,3 +97,59 @@ def test_benchmark_config2_sampled_rows(device):
         assert_attention_close(got, ref, torch.bfloat16)
         assert_lse_close(got_lse, refl)
     assert torch.isfinite(out).all() and torch.isfinite(lse).all()
+
+
+@pytest.mark.parametrize("window,causal", [((1024, 0), True), ((0, 0), True), ((15, 2), False),
+                                           ((-1, 7), False), ((127, -1), True), ((300, 40), False)])
+def test_windows_on_tensor_core_path(device, window, causal):
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_attention
+    lens = [1, 200, 700, 1500, 129]
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(sum(lens), 8, 128, generator=g).to(torch.bfloat16).to(device)
+    k = torch.randn(sum(lens), 2, 128, generator=g).to(torch.bfloat16).to(device)
+    v = torch.randn(sum(lens), 2, 128, generator=g).to(torch.bfloat16).to(device)
+    c = cu(lens, device)
+    sinks = torch.linspace(-2, 2, 8, device=device)
+    out, lse = vllm_attention(q, k, v, max(lens), c, max(lens), cu_seqlens_k=c, causal=causal,
+                              window_size=list(window), s_aux=sinks, return_softmax_lse=True)
+    ref, refl = reference(q, k, v, c, c, causal=causal, window=window, sinks=sinks)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
+
+
+@pytest.mark.parametrize("cap", [0.25, 1.0, 50.0])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_softcap_on_tensor_core_path(device, cap, dtype):
+    lens = [100, 333, 1024]
+    g = torch.Generator().manual_seed(11)
+    q = (torch.randn(sum(lens), 4, 128, generator=g) * 3).to(dtype).to(device)
+    k = (torch.randn(sum(lens), 4, 128, generator=g) * 3).to(dtype).to(device)
+    v = torch.randn(sum(lens), 4, 128, generator=g).to(dtype).to(device)
+    c = cu(lens, device)
+    out, lse = flash_attn_varlen_func(q, k, v, c, c, max(lens), max(lens), causal=True, softcap=cap,
+                                      window_size=(1024, 0) if cap == 50.0 else (-1, -1),
+                                      return_softmax_lse=True)
+    ref, refl = reference(q, k, v, c, c, causal=True, softcap=cap,
+                          window=(1024, 0) if cap == 50.0 else (-1, -1))
+    assert_attention_close(out, ref, dtype)
+    assert_lse_close(lse, refl)
+
+
+def test_dynamic_causal_and_descales_on_tensor_core_path(device):
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_attention
+    qlens, klens = [5, 300, 257], [400, 300, 600]
+    g = torch.Generator().manual_seed(13)
+    q = torch.randn(sum(qlens), 8, 128, generator=g).to(torch.float16).to(device)
+    k = torch.randn(sum(klens), 4, 128, generator=g).to(torch.float16).to(device)
+    v = torch.randn(sum(klens), 4, 128, generator=g).to(torch.float16).to(device)
+    cq, ck = cu(qlens, device), cu(klens, device)
+    dyn = torch.tensor([True, False, True], device=device)
+    qs = torch.tensor([[.5], [.75], [1.]], device=device).expand(3, 4)
+    ks = torch.tensor([[.4, .6, 1.1, .9]], device=device).expand(3, 4)
+    vs = torch.tensor([[.2, .9, 1., 1.5]], device=device).expand(3, 4)
+    out, lse = vllm_attention(q, k, v, max(qlens), cq, max(klens), cu_seqlens_k=ck, causal=True,
+                              dynamic_causal=dyn, q_descale=qs, k_descale=ks, v_descale=vs,
+                              return_softmax_lse=True)
+    ref, refl = reference(q, k, v, cq, ck, causal=dyn, q_descale=qs, k_descale=ks, v_descale=vs)
+    assert_attention_close(out, ref)
+    assert_lse_close(lse, refl)
