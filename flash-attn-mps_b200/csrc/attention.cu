@@ -188,6 +188,8 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
     if (!a->deterministic && a->num_splits <= 1 && prefill_sm100_supported(p)) {
       plan->route = kRoutePrefill;
       plan->splits = 1;
+      plan->part_bytes = 256;  // persistent-scheduler work counter
+      return FA_OK;
     } else {
       const bool vector = a->deterministic || a->max_seqlen_q == 1 || std::max(p.DQ, p.DV) > 256;
       plan->splits = a->deterministic ? 1
@@ -236,6 +238,12 @@ extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
   rc = make_plan(a, p, &plan);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (plan.route == kRoutePrefill) {
+    FAB_CHECK_ARG(present(a->workspace) && a->workspace.ndim >= 1 &&
+                      (size_t)a->workspace.shape[0] * elem_size(a->workspace.dtype) >= plan.part_bytes,
+                  "workspace smaller than fa_attention_workspace_size");
+    p.scratch = a->workspace.ptr;
+  }
   if (plan.splits > 1) {
     FAB_CHECK_ARG(present(a->workspace) && a->workspace.ndim >= 1 &&
                       (size_t)a->workspace.shape[0] * elem_size(a->workspace.dtype) >= plan.part_bytes + plan.lse_bytes,

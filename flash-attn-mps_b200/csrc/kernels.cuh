@@ -28,6 +28,7 @@ struct AttnParams {
   void* out; int32_t ot; int64_t os0, os1, os2;
   float* lse; int64_t ls0, ls1;    // [H,T]
   float* part; float* part_lse;    // split workspace (contiguous) or null
+  void* scratch;                   // prefill: work counter (zeroed before launch)
   const int32_t* cu_q; int64_t cq0;
   const int32_t* cu_k; int64_t ck0;
   const int32_t* used; int64_t u0;
