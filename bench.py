@@ -184,7 +184,6 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     import torch.distributed as dist
     from flash_attn_b200 import store_kvcache
     from flash_attn_b200._attention import attention
-    from flash_attn_b200._merge import _merge_partials
 
     cfg = dict(CFG4)
     B, C, HQ, HK, D = cfg["batch"], cfg["ctx"], cfg["hq"], cfg["hkv"], cfg["d"]
@@ -199,23 +198,21 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     cu_q = torch.arange(B + 1, dtype=torch.int32, device=dev)
     used = torch.full((B,), shard, dtype=torch.int32, device=dev)
     sinks = None
-    partial = torch.empty(B, HQ, D, dtype=torch.float32, device=dev)
-    gathered = torch.empty(world, B, HQ, D, dtype=torch.float32, device=dev)
-    gathered_lse = torch.empty(world, HQ, B, dtype=torch.float32, device=dev)
     out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
-    out_lse = torch.empty(HQ, B, dtype=torch.float32, device=dev)
+    partial = torch.empty(B, HQ, D, dtype=torch.float32, device=dev)
+    decoder = None
+    if world > 1:
+        from flash_attn_b200.distributed import ShardedDecoder
+        decoder = ShardedDecoder(B, HQ, D, torch.bfloat16, dev)
 
     def step(q_in):
         if world == 1:
             return attention(q_in, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
                              max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
                              s_aux=sinks, out=out)
-        o, l = attention(q_in, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
-                         max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
-                         out=partial)
-        dist.all_gather_into_tensor(gathered.view(world, -1), o.reshape(-1))
-        dist.all_gather_into_tensor(gathered_lse.view(world, -1), l.reshape(-1))
-        return _merge_partials(gathered, gathered_lse, out=out, out_lse=out_lse)
+        return decoder.step(q_in, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used,
+                            max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd,
+                            s_aux=sinks)
 
     # ---- device-resident timing --------------------------------------------
     for _ in range(args.warmup):

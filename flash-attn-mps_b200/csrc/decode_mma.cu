@@ -430,6 +430,11 @@ template <typename MT, bool FP8, int D>
 int launch_heads(const AttnParams& p, int splits, int span, bool prec, bool qfold, cudaStream_t st) {
   const bool wide = p.HQ / p.HK > 8;
   if (qfold) {
+    // bf16 queries over FP8 K/V: scale folded into f16 query fragments; an
+    // fp32 output (e.g. a multi-GPU partial) also keeps P to ~22 bits.
+    if (prec)
+      return wide ? launch_cfg<MT, FP8, D, 16, true, true>(p, splits, span, st)
+                  : launch_cfg<MT, FP8, D, 8, true, true>(p, splits, span, st);
     return wide ? launch_cfg<MT, FP8, D, 16, false, true>(p, splits, span, st)
                 : launch_cfg<MT, FP8, D, 8, false, true>(p, splits, span, st);
   }
@@ -461,9 +466,6 @@ int decode_mma_supported(const AttnParams& p) {
   const int64_t ks[3] = {p.ks0, p.ks1, p.ks2}, vs[3] = {p.vs0, p.vs1, p.vs2};
   for (int i = p.paged ? 0 : 1; i < 3; ++i)
     if ((ks[i] * elt) % 16 != 0 || (vs[i] * elt) % 16 != 0) return 0;
-  // bf16 queries with FP8 K/V fold the score scale into f16 queries; an fp32
-  // output asks for the reference's fp32-exact path instead.
-  if (fp8 && p.qt == FA_BF16 && p.ot == FA_F32) return 0;
   if (p.B > 65535 || p.HK * ((p.HQ / p.HK + 15) / 16) > 65535) return 0;
   return 1;
 }
