@@ -16,7 +16,7 @@ with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
 that token, attention, D2H of the output.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_decode|decode|prefill]
+                    [--workload fp8_decode|prefill|prefill_softcap_window|bf16_decode] [--small]
 """
 
 import argparse
@@ -179,6 +179,17 @@ def cfg4_bytes(cfg):
     return kv + table + qo
 
 
+def profiled_traffic(name, key="traffic_bytes_per_full_launch"):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/ (or None)."""
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith(key + ":"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
 def run_fp8_decode(args, rank, world, peaks, peak_kind):
     import torch
     import torch.distributed as dist
@@ -186,6 +197,8 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     from flash_attn_b200._attention import attention
 
     cfg = dict(CFG4)
+    if args.small:
+        cfg["ctx"] = 8192  # profiling case: 1.07 GB of FP8 cache, still far larger than L2
     B, C, HQ, HK, D = cfg["batch"], cfg["ctx"], cfg["hq"], cfg["hkv"], cfg["d"]
     shard = C // world
     dev = torch.device("cuda")
@@ -289,10 +302,14 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
         "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel (+ its split merge)",
                      "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved_gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)",
-                     "traffic": None, "algorithmic_bytes_per_launch": rank_bytes,
+                     "traffic": (profiled_traffic("decode_mma_fp8_cfg4.md") / world
+                                 if profiled_traffic("decode_mma_fp8_cfg4.md") and not args.small else None),
+                     "traffic_source": "profiles/decode_mma_fp8_cfg4.md (ncu dram__bytes_read+write, small case scaled)",
+                     "algorithmic_bytes_per_launch": rank_bytes,
                      "kernel_ms": kernel_ms},
         "dtype": "fp8_e4m3 KV / bf16 q, fp32 softmax",
-        "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode, split-KV, KV sharded over ranks",
+        "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode, split-KV, KV sharded over ranks"
+                               + (" (small profiling case)" if args.small else ""),
                    "batch": B, "context": C, "block_size": cfg["page"], "q_heads": HQ, "kv_heads": HK,
                    "head_dim": D, "kv_bytes_total": B * C * HK * 2 * D,
                    "l2": "inputs (17.2 GB cache) larger than L2; no flush needed",
@@ -340,11 +357,13 @@ def time_loop(fn, steps, warmup):
     return s.elapsed_time(e) / steps
 
 
-def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1)):
+def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func."""
     import torch
     from flash_attn_b200 import flash_attn_varlen_func
     cfg = dict(CFG2)
+    if small:
+        cfg["seqs"] = 4  # profiling case
     lens = cfg2_lengths(cfg)
     total = sum(lens)
     dev = torch.device("cuda")
@@ -368,12 +387,14 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
                          "frac_of_sustained": tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
 
 
-def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5):
+def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False):
     """Config 3: paged bf16 decode, B=256, ctx ~U[512, 32768], page 16."""
     import numpy as np
     import torch
     from flash_attn_b200._attention import attention
     cfg = dict(CFG3)
+    if small:
+        cfg["batch"] = 16  # profiling case
     rng = np.random.default_rng(cfg["seed"])
     ctx = rng.integers(cfg["cmin"], cfg["cmax"] + 1, size=cfg["batch"])
     P = cfg["page"]
@@ -473,7 +494,9 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_decode"], default="fp8_decode")
+    ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "bf16_decode"],
+                    default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
+    ap.add_argument("--small", action="store_true", help="shrunken workload for ncu captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-2/3 measurements")
     args = ap.parse_args()
@@ -487,6 +510,25 @@ def main():
     import torch
     rank, world, local = dist_setup(args.gpus)
     peaks, peak_kind = load_peaks()
+    if args.workload != "fp8_decode":
+        # Single-workload runs (profiling and secondary measurements), rank 0 only.
+        if rank == 0:
+            if args.workload == "prefill":
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload == "prefill_softcap_window":
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, softcap=50.0,
+                                window=(1024, 0), small=args.small)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
+            else:
+                r = run_bf16_decode(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small)
+                value, unit = r["TB/s"], "TB/s"
+            print(json.dumps({"metric": METRIC, "value": value, "unit": unit, "n_gpus": 1,
+                              "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                              "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                              "dtype": "bf16", "data": "synthetic (seeded)",
+                              "config": {"workload": r["workload"]}, "roofline": r["roofline"]}))
+        return
     res = run_fp8_decode(args, rank, world, peaks, peak_kind)
     if rank == 0:
         line = {"metric": METRIC, "value": res["value"], "unit": res["unit"], "n_gpus": world,
@@ -495,10 +537,12 @@ def main():
                 "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"],
                 "e2e": res["e2e"], "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
                 "clocks": res["clocks"]}
-        if world == 1 and not args.no_secondary:
+        if world == 1 and not args.no_secondary and not args.small:
             line["secondary"] = {"prefill_cfg2": run_prefill(peaks, peak_kind),
+                                 "prefill_cfg2_softcap_window": run_prefill(peaks, peak_kind, softcap=50.0,
+                                                                            window=(1024, 0)),
                                  "decode_cfg3": run_bf16_decode(peaks, peak_kind)}
-        if world == 1 and not args.no_cpu_baseline:
+        if world == 1 and not args.no_cpu_baseline and not args.small:
             line["cpu_baseline"] = cpu_baseline_block(CFG4)
         print(json.dumps(line))
     if world > 1:
