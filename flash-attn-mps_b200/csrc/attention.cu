@@ -11,6 +11,10 @@
 //     (_attention.py:241-243).
 // The choice depends on shapes, dtypes, strides and flags only, never on
 // tensor values or lengths beyond the caller's max_seqlen_*.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "kernels.cuh"
 
 namespace fab {
@@ -40,6 +44,47 @@ int sm_count() {
     cached[dev] = n;
   }
   return cached[dev];
+}
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+}  // namespace
+
+bool tensor_map_available() { return encode_fn() != nullptr; }
+
+int encode_tensor_map(void* map, int dtype, int rank, const void* ptr, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMapDataType t = dtype == FA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                          : dtype == FA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(map), t, (cuuint32_t)rank, const_cast<void*>(ptr), d, st, bx, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FA_OK;
 }
 
 namespace {
@@ -108,6 +153,7 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
     p->ks0 = k.stride[0]; p->ks1 = k.stride[1]; p->ks2 = k.stride[2]; p->ks3 = k.stride[3];
     p->vs0 = v.stride[0]; p->vs1 = v.stride[1]; p->vs2 = v.stride[2]; p->vs3 = v.stride[3];
     p->page = (int32_t)k.shape[1];
+    p->k_pages = k.shape[0];
     p->paged = 1;
   } else {
     p->ks1 = k.stride[0]; p->ks2 = k.stride[1]; p->ks3 = k.stride[2];
@@ -124,6 +170,7 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
   if (present(a->block_table)) {
     p->table = reinterpret_cast<const int32_t*>(a->block_table.ptr);
     p->bt0 = a->block_table.stride[0]; p->bt1 = a->block_table.stride[1];
+    p->bt_cols = a->block_table.shape[1];
   }
   if (present(a->leftpad_k)) { p->leftpad = reinterpret_cast<const int32_t*>(a->leftpad_k.ptr); p->lp0 = a->leftpad_k.stride[0]; }
   if (present(a->causal_per_seq)) {
@@ -212,6 +259,13 @@ using namespace fab;
 extern "C" int fa_abi_version(void) { return FA_B200_ABI_VERSION; }
 
 extern "C" const char* fa_last_error(void) { return last_error().c_str(); }
+
+extern "C" int fa_pipeline_timeouts(int clear) {
+  const int a = fab::prefill_timeout_flag(clear != 0);
+  const int b = fab::decode_timeout_flag(clear != 0);
+  if (a < 0 || b < 0) return -1;
+  return (a ? 1 : 0) | (b ? 2 : 0);
+}
 
 extern "C" int fa_attention_workspace_size(const fa_attention_args* a, size_t* bytes) {
   FAB_CHECK_ARG(bytes != nullptr, "bytes must not be null");

@@ -26,12 +26,17 @@
 // FP8 decode at 9-16) and its dispatcher (flash_attn_mps/_decode.py:40-99).
 #include "kernels.cuh"
 #include "ptx.cuh"
+#include "sm100.cuh"
 
 namespace fab {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
+
+// Set by a TMA-pipeline wait that gave up (a bounded mbarrier wait); the host
+// reads it through decode_timeout_flag().
+__device__ int g_decode_timeout;
 
 template <bool FP8, int D, int W, int NH>
 struct Geometry {
@@ -41,7 +46,14 @@ struct Geometry {
   static constexpr int kStageBytes = 2 * kTile * kRowBytes;
   static constexpr int kN8 = NH / 8;                   // head tiles
   static constexpr int kDT = D / 16;                   // 16-row output tiles per head tile
+  static constexpr int kHalves = kRowBytes / 128;      // 128-byte column blocks of a row
   static_assert(kChunks >= 8 && kChunks % 8 == 0, "rows must span whole 128-byte swizzle atoms");
+  // Byte offset of 16-byte chunk c of token row r inside a K or V stage tile:
+  // [column block][row][128 B], chunks XOR-swizzled by (r & 7) -- the layout
+  // TMA's 128-byte swizzle writes into a 1024-byte-aligned tile.
+  static __device__ __forceinline__ uint32_t off(int r, int c) {
+    return (uint32_t)((((c >> 3) * kTile + r) << 7) + (((c & 7) ^ (r & 7)) << 4));
+  }
 };
 
 // Head-dimension index of row (g or g+8) of output tile j.
@@ -56,11 +68,15 @@ __device__ __forceinline__ int out_dim(int j, int row) {
   }
 }
 
-template <typename MT, bool FP8, int D, int W, int NH, int NST, bool PREC, bool QFOLD, int MINB>
-__global__ void __launch_bounds__(W * 32, MINB)
-    decode_mma_kernel(const AttnParams p, const int span, const int hblocks, const int page_shift) {
+template <typename MT, bool FP8, int D, int W, int NH, int NST, bool PREC, bool QFOLD, bool TMA, int MINB>
+__global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
+    decode_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      const AttnParams p, const int span, const int hblocks, const int page_shift,
+                      const int box_tok) {
   using G = Geometry<FP8, D, W, NH>;
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);  // 1024-aligned tiles
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, qd = lane & 3;
   const int split = blockIdx.x;
@@ -127,6 +143,23 @@ __global__ void __launch_bounds__(W * 32, MINB)
   }
 
   // ---- K/V gather -----------------------------------------------------------
+  // Tile it covers logical cache positions [L0 + it*kTile, +kTile); the TMA
+  // path aligns L0 down to the tile size so whole pages arrive as boxes.
+  const int L0 = TMA ? ((begin + left) / G::kTile) * G::kTile : begin + left;
+  const int n_tiles = end > begin ? (end + left - L0 + G::kTile - 1) / G::kTile : 0;
+  const uint32_t bar_base = smem_u32(smem) + NST * G::kStageBytes;
+  auto full_bar = [&](int s_) { return bar_base + 8u * (uint32_t)s_; };
+  auto empty_bar = [&](int s_) { return bar_base + 8u * (uint32_t)(NST + s_); };
+  if constexpr (TMA) {
+    if (tid == 0) {
+      for (int s_ = 0; s_ < NST; ++s_) {
+        sm100::mbar_init(full_bar(s_), 1);
+        sm100::mbar_init(empty_bar(s_), W);
+      }
+      sm100::mbar_fence_init();
+    }
+    __syncthreads();
+  }
   const int elt = FP8 ? 1 : 2;
   const uint8_t* kglob = reinterpret_cast<const uint8_t*>(p.k) + (int64_t)kh * p.ks2 * elt;
   const uint8_t* vglob = reinterpret_cast<const uint8_t*>(p.v) + (int64_t)kh * p.vs2 * elt;
@@ -154,33 +187,91 @@ __global__ void __launch_bounds__(W * 32, MINB)
           voff = (int64_t)logical * p.vs1;
         }
       }
-      const uint32_t sw = (uint32_t)((c ^ (r & 7)) << 4);
-      cp_async_16(smem_u32(ks + r * G::kRowBytes) + sw, kglob + koff * elt + c * 16, ok ? 16 : 0);
-      cp_async_16(smem_u32(vs + r * G::kRowBytes) + sw, vglob + voff * elt + c * 16, ok ? 16 : 0);
+      const uint32_t o = G::off(r, c);
+      cp_async_16(smem_u32(ks) + o, kglob + koff * elt + c * 16, ok ? 16 : 0);
+      cp_async_16(smem_u32(vs) + o, vglob + voff * elt + c * 16, ok ? 16 : 0);
     }
   };
 
-  const int n_tiles = end > begin ? (end - begin + G::kTile - 1) / G::kTile : 0;
+  if constexpr (TMA) {
+    if (warp == W) {
+      // ---------------------------------------------------- TMA producer warp
+      // One box = box_tok consecutive tokens of one page (128 bytes of each row
+      // per box); boxes of pages past the sequence use page -1, which TMA
+      // treats as out of bounds and fills with zeros.
+      const int nbox = G::kTile / box_tok;
+      const int total = 2 * G::kHalves * nbox;
+      int issued = 0;
+      for (int it = 0; it < n_tiles; ++it) {
+        const int st = it % NST;
+        if (it >= NST) {
+          const bool ok = sm100::mbar_wait(empty_bar(st), ((it / NST) - 1) & 1, &g_decode_timeout);
+          if (!__all_sync(0xffffffffu, ok)) break;
+        }
+        if (lane == 0) sm100::mbar_expect_tx(full_bar(st), G::kStageBytes);
+        __syncwarp();
+        const int lb = L0 + it * G::kTile;
+        const uint32_t sbase = smem_u32(smem) + st * G::kStageBytes;
+        for (int i = lane; i < total; i += 32) {
+          const int tensor = i / (G::kHalves * nbox);
+          const int rem = i - tensor * G::kHalves * nbox;
+          const int half = rem / nbox, bx = rem - half * nbox;
+          const int logical = lb + bx * box_tok;
+          const int pg = logical >> page_shift;
+          int blk = -1;
+          if (logical - left < len && pg < p.bt_cols) blk = __ldg(trow + (int64_t)pg * p.bt1);
+          const uint32_t dst = sbase + tensor * (G::kTile * G::kRowBytes) + (uint32_t)((half * G::kTile + bx * box_tok) << 7);
+          sm100::tma_load_4d(dst, tensor ? &tmv : &tmk, full_bar(st), half * (128 / elt), kh,
+                             logical & (p.page - 1), blk);
+        }
+        __syncwarp();
+        issued = it + 1;
+      }
+      // Every issued load must land before the CTA leaves.
+      for (int it = max(0, issued - NST); it < issued; ++it)
+        sm100::mbar_wait(full_bar(it % NST), (it / NST) & 1, &g_decode_timeout);
+    }
+  } else {
 #pragma unroll
-  for (int s = 0; s < NST - 1; ++s) {
-    if (s < n_tiles) load_stage(s, begin + s * G::kTile);
-    cp_async_commit();
-  }
-
-  for (int it = 0; it < n_tiles; ++it) {
-    cp_async_wait<NST - 2>();
-    __syncthreads();
-    {
-      const int nxt = it + NST - 1;
-      if (nxt < n_tiles) load_stage(nxt % NST, begin + nxt * G::kTile);
+    for (int s_ = 0; s_ < NST - 1; ++s_) {
+      if (s_ < n_tiles) load_stage(s_, L0 - left + s_ * G::kTile);
       cp_async_commit();
     }
-    const int t0 = begin + it * G::kTile + warp * 16;
-    if (t0 >= end) continue;
+  }
+
+  for (int it = 0; it < n_tiles && (!TMA || warp < W); ++it) {
+    if constexpr (!TMA) {
+      cp_async_wait<NST - 2>();
+      __syncthreads();
+      const int nxt = it + NST - 1;
+      if (nxt < n_tiles) load_stage(nxt % NST, L0 - left + nxt * G::kTile);
+      cp_async_commit();
+    } else {
+      const bool ok = sm100::mbar_wait(full_bar(it % NST), (it / NST) & 1, &g_decode_timeout);
+      if (!__all_sync(0xffffffffu, ok)) break;
+    }
+    const int t0 = L0 - left + it * G::kTile + warp * 16;
+    const bool any = t0 + 16 > begin && t0 < end;
     const uint32_t kbase = smem_u32(smem + (it % NST) * G::kStageBytes);
     const uint32_t vbase = kbase + G::kTile * G::kRowBytes;
     const int wt0 = warp * 16;
-
+    if (TMA && any && !(t0 >= begin && t0 + 16 <= end)) {
+      // Rows of this warp outside [begin, end) came from whole-page boxes:
+      // zero their V rows so a NaN-poisoned slot never meets a zero weight.
+      const int rr = lane & 15, part = lane >> 4;
+      if (t0 + rr < begin || t0 + rr >= end) {
+#pragma unroll
+        for (int hf = 0; hf < G::kHalves; ++hf)
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            *reinterpret_cast<uint4*>(smem + (it % NST) * G::kStageBytes + G::kTile * G::kRowBytes +
+                                      ((hf * G::kTile + wt0 + rr) << 7) + part * 64 + q4 * 16) = make_uint4(0, 0, 0, 0);
+        // Order these generic stores before the next TMA write of the slot.
+        sm100::fence_proxy_async_smem();
+      }
+      __syncwarp();
+    }
+    if (any) {
     // S^T = K Q^T over this warp's 16 tokens, as two independent MMA chains.
     float s[G::kN8][4], s2[G::kN8][4];
 #pragma unroll
@@ -190,13 +281,12 @@ __global__ void __launch_bounds__(W * 32, MINB)
     {
       const int mi = lane >> 3;
       const int tok = wt0 + (mi & 1) * 8 + (lane & 7);
-      const uint32_t rowaddr = kbase + tok * G::kRowBytes;
       if constexpr (!FP8) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const int ch = kk * 2 + (mi >> 1);
           uint32_t a[4];
-          ldsm_x4(rowaddr + ((ch ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+          ldsm_x4(kbase + G::off(tok, ch), a[0], a[1], a[2], a[3]);
 #pragma unroll
           for (int n8 = 0; n8 < G::kN8; ++n8) {
             if (kk & 1) mma16816<MT>(s2[n8], a, qb[n8][kk][0], qb[n8][kk][1]);
@@ -208,7 +298,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
         for (int kc = 0; kc < D / 32; ++kc) {
           const int ch = 2 * kc + (mi >> 1);
           uint32_t r0, r1, r2, r3;
-          ldsm_x4(rowaddr + ((ch ^ (tok & 7)) << 4), r0, r1, r2, r3);
+          ldsm_x4(kbase + G::off(tok, ch), r0, r1, r2, r3);
           uint32_t a0[4], a1[4];
           e4m3x4_to_f16x2x2(r0, a0[0], a0[2]);
           e4m3x4_to_f16x2x2(r1, a0[1], a0[3]);
@@ -229,8 +319,8 @@ __global__ void __launch_bounds__(W * 32, MINB)
 
     // Online softmax per head column (log2 domain). Element e of tile n8:
     // token (e < 2 ? g : g + 8), head column 2*qd + (e & 1).
-    const bool full = t0 + 16 <= end;
-    const bool tok_lo = t0 + g < end, tok_hi = t0 + g + 8 < end;
+    const bool full = t0 >= begin && t0 + 16 <= end;
+    const bool tok_lo = t0 + g >= begin && t0 + g < end, tok_hi = t0 + g + 8 >= begin && t0 + g + 8 < end;
     bool changed = false;
     uint32_t pb[G::kN8][2], pl[G::kN8][2];
 #pragma unroll
@@ -288,13 +378,12 @@ __global__ void __launch_bounds__(W * 32, MINB)
     {
       const int mi = lane >> 3;
       const int tok = wt0 + (mi >> 1) * 8 + (lane & 7);
-      const uint32_t rowaddr = vbase + tok * G::kRowBytes;
       if constexpr (!FP8) {
 #pragma unroll
         for (int j = 0; j < G::kDT; ++j) {
           const int ch = j * 2 + (mi & 1);
           uint32_t a[4];
-          ldsm_x4_t(rowaddr + ((ch ^ (tok & 7)) << 4), a[0], a[1], a[2], a[3]);
+          ldsm_x4_t(vbase + G::off(tok, ch), a[0], a[1], a[2], a[3]);
 #pragma unroll
           for (int n8 = 0; n8 < G::kN8; ++n8) {
             mma16816<MT>(o[n8][j], a, pb[n8][0], pb[n8][1]);
@@ -306,7 +395,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
         for (int jg = 0; jg < D / 32; ++jg) {
           const int ch = jg * 2 + (mi & 1);
           uint32_t r[4];
-          ldsm_x4_t(rowaddr + ((ch ^ (tok & 7)) << 4), r[0], r[1], r[2], r[3]);
+          ldsm_x4_t(vbase + G::off(tok, ch), r[0], r[1], r[2], r[3]);
           // Bytes (0,2) are one output dim over two tokens, (1,3) the next dim.
           uint32_t ae[4], ao[4];
 #pragma unroll
@@ -323,8 +412,13 @@ __global__ void __launch_bounds__(W * 32, MINB)
         }
       }
     }
+    }  // any
+    if constexpr (TMA) {
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(empty_bar(it % NST));
+    }
   }
-  cp_async_wait<0>();
+  if constexpr (!TMA) cp_async_wait<0>();
   __syncthreads();
 
   // ---- merge the warps' states through shared memory -------------------------
@@ -332,7 +426,7 @@ __global__ void __launch_bounds__(W * 32, MINB)
   float* cl = cm + W * NH;                      // [W][NH]
   float* co = cl + W * NH;                      // [W][NH][D]
 #pragma unroll
-  for (int n8 = 0; n8 < G::kN8; ++n8) {
+  for (int n8 = 0; n8 < G::kN8 && warp < W; ++n8) {
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
       float x = l[n8][c];
@@ -394,12 +488,14 @@ __global__ void __launch_bounds__(W * 32, MINB)
   }
 }
 
+// Stage ring + its 2*NST mbarriers (the warp merge reuses the ring), plus
+// slack to align the ring to 1024 bytes for the 128-byte TMA swizzle.
 template <bool FP8, int D, int W, int NH>
 constexpr int smem_bytes(int nst) {
   using G = Geometry<FP8, D, W, NH>;
   const int pipe = nst * G::kStageBytes;
   const int merge = (2 * W * NH + W * NH * D) * 4;
-  return pipe > merge ? pipe : merge;
+  return (pipe > merge ? pipe : merge) + 16 * nst + 1024;
 }
 
 int page_shift_of(const AttnParams& p) {
@@ -409,19 +505,83 @@ int page_shift_of(const AttnParams& p) {
   return s;
 }
 
+// CTA shape: warps per CTA (16 tokens each per stage), pipeline stages and the
+// occupancy bound, per K/V storage type.
+#ifndef FAB_DECODE_FP8_W
+#define FAB_DECODE_FP8_W 8
+#endif
+#ifndef FAB_DECODE_FP8_NST
+#define FAB_DECODE_FP8_NST 3
+#endif
+#ifndef FAB_DECODE_FP8_MINB
+#define FAB_DECODE_FP8_MINB 2
+#endif
+#ifndef FAB_DECODE_16_W
+#define FAB_DECODE_16_W 4
+#endif
+#ifndef FAB_DECODE_16_NST
+#define FAB_DECODE_16_NST 3
+#endif
+#ifndef FAB_DECODE_16_MINB
+#define FAB_DECODE_16_MINB 2
+#endif
+#ifndef FAB_DECODE_MIN_SPLITS
+#define FAB_DECODE_MIN_SPLITS 4
+#endif
+#ifndef FAB_DECODE_TMA
+#define FAB_DECODE_TMA 1
+#endif
+
+// TMA page gathers: paged K/V whose pages are whole 1024-byte swizzle atoms
+// (page >= 8 tokens, power of two) and whose strides suit a tensor map. Odd
+// page sizes and packed K/V keep the per-row cp.async gather.
+bool use_tma(const AttnParams& p, int page_shift) {
+  if (!FAB_DECODE_TMA || !p.paged || page_shift < 3 || !tensor_map_available()) return false;
+  const int64_t elt = p.kt == FA_E4M3 ? 1 : 2;
+  const int64_t lim = (int64_t)1 << 40;
+  for (int64_t st : {p.ks0, p.ks1, p.ks2, p.vs0, p.vs1, p.vs2})
+    if (st <= 0 || (st * elt) % 16 != 0 || st * elt >= lim) return false;
+  return p.k_pages > 0 && p.k_pages < ((int64_t)1 << 31);
+}
+
+// 4-D map over one K or V cache: (head dim, kv head, token in page, page).
+int make_page_map(CUtensorMap* map, const void* base, int dtype, const AttnParams& p, bool is_v, int box_tok) {
+  const int64_t elt = dtype == FA_E4M3 ? 1 : 2;
+  const int D = is_v ? p.DV : p.DQ;
+  const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p.HK, (uint64_t)p.page, (uint64_t)p.k_pages};
+  const uint64_t strides[3] = {(uint64_t)((is_v ? p.vs2 : p.ks2) * elt), (uint64_t)((is_v ? p.vs1 : p.ks1) * elt),
+                               (uint64_t)((is_v ? p.vs0 : p.ks0) * elt)};
+  const uint32_t box[4] = {(uint32_t)(128 / elt), 1u, (uint32_t)box_tok, 1u};
+  return encode_tensor_map(map, dtype, 4, base, dims, strides, box, true);
+}
+
 template <typename MT, bool FP8, int D, int NH, bool PREC, bool QFOLD>
 int launch_cfg(const AttnParams& p, int splits, int span, cudaStream_t stream) {
-  constexpr int W = FP8 ? 8 : 4;
-  constexpr int NST = 3;
-  constexpr int MINB = (FP8 && NH == 16) ? 1 : 2;
+  constexpr int W = FP8 ? FAB_DECODE_FP8_W : FAB_DECODE_16_W;
+  constexpr int NST = FP8 ? FAB_DECODE_FP8_NST : FAB_DECODE_16_NST;
+  constexpr int MINB = (FP8 && NH == 16) ? 1 : (FP8 ? FAB_DECODE_FP8_MINB : FAB_DECODE_16_MINB);
   constexpr int smem = smem_bytes<FP8, D, W, NH>(NST);
-  auto kernel = decode_mma_kernel<MT, FP8, D, W, NH, NST, PREC, QFOLD, MINB>;
+  const int shift = page_shift_of(p);
+  const bool tma = use_tma(p, shift);
+  auto kernel = tma ? decode_mma_kernel<MT, FP8, D, W, NH, NST, PREC, QFOLD, true, MINB>
+                    : decode_mma_kernel<MT, FP8, D, W, NH, NST, PREC, QFOLD, false, MINB>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "decode smem attribute: %s", cudaGetErrorString(e));
   const int group = p.HQ / p.HK;
   const int hblocks = (group + NH - 1) / NH;
+  constexpr int kTile = Geometry<FP8, D, W, NH>::kTile;
+  const int box_tok = tma ? min(p.page, kTile) : 0;
+  CUtensorMap tmk, tmv;
+  memset(&tmk, 0, sizeof(tmk));
+  memset(&tmv, 0, sizeof(tmv));
+  if (tma) {
+    const int kd = FP8 ? FA_E4M3 : p.kt;
+    int rc = make_page_map(&tmk, p.k, kd, p, false, box_tok);
+    if (rc == FA_OK) rc = make_page_map(&tmv, p.v, kd, p, true, box_tok);
+    if (rc != FA_OK) return rc;
+  }
   dim3 grid((unsigned)splits, (unsigned)(p.HK * hblocks), (unsigned)p.B);
-  kernel<<<grid, W * 32, smem, stream>>>(p, span, hblocks, page_shift_of(p));
+  kernel<<<grid, (W + (tma ? 1 : 0)) * 32, smem, stream>>>(tmk, tmv, p, span, hblocks, shift, box_tok);
   FAB_LAUNCH_CHECK("decode launch");
   return FA_OK;
 }
@@ -448,7 +608,7 @@ int launch_heads(const AttnParams& p, int splits, int span, bool prec, bool qfol
 
 bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
-int tile_tokens(const AttnParams& p) { return p.kt == FA_E4M3 ? 16 * 8 : 16 * 4; }
+int tile_tokens(const AttnParams& p) { return p.kt == FA_E4M3 ? 16 * FAB_DECODE_FP8_W : 16 * FAB_DECODE_16_W; }
 
 }  // namespace
 
@@ -476,10 +636,23 @@ int decode_default_splits(const AttnParams& p, int* span) {
   const int64_t units = (int64_t)p.B * p.HK * ((group + 15) / 16);
   const int by_len = max(1, (eff + 255) / 256);
   const int want = (int)((8LL * sm_count() + units - 1) / units);
-  int splits = max(want, (eff + 4095) / 4096);
+  // Few long splits amortise each CTA's prologue and pipeline fill (measured:
+  // 4 splits beat 8..32 on both uniform 131072-token and ragged 512..32768
+  // contexts); more splits only when the grid would not fill the SMs.
+  int splits = max(want, FAB_DECODE_MIN_SPLITS);
   splits = max(1, min(splits, by_len));
   *span = (eff + splits - 1) / splits;
   return splits;
+}
+
+int decode_timeout_flag(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_decode_timeout, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_decode_timeout, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
 }
 
 int launch_decode_mma(const AttnParams& p, int splits, int span, cudaStream_t stream) {

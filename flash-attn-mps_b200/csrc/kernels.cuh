@@ -15,6 +15,12 @@ struct MergePartialsArgs {
 };
 int launch_merge_partials(const MergePartialsArgs& a, cudaStream_t stream);
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda
+// link dependency). rank <= 5; strides in bytes for dims 1..rank-1.
+bool tensor_map_available();
+int encode_tensor_map(void* map, int dtype, int rank, const void* ptr, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, bool swizzle128);
+
 // Flattened attention parameters: device pointers, element strides and
 // feature flags. Mirrors the reference's parameter vector
 // (flash_attn_mps/_attention.py:10-16 _META, filled at 265-295).
@@ -44,6 +50,7 @@ struct AttnParams {
   const int32_t* mp; int64_t mp0;        // mask kind 2 prefix [B]
   const int32_t* mw;                      // mask kind 2 window [1]
   int64_t k_rows;                        // packed K/V: rows of the K/V tensors
+  int64_t k_pages, bt_cols;              // paged K/V: pages in the cache, block_table columns
   int32_t T, B, HQ, HK, DQ, DV, page;
   int32_t paged, causal, dynamic, win_l, win_r;
   int32_t mask, mask_win, clamp, splits, max_q, max_k;
@@ -62,5 +69,9 @@ int decode_default_splits(const AttnParams& p, int* span);
 // tcgen05/TMEM/TMA prefill kernel.
 int prefill_sm100_supported(const AttnParams& p);
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream);
+// Timed-out pipeline waits recorded by the prefill / TMA decode kernels on the
+// current device (1 = some wait gave up, 0 = none, -1 = CUDA error).
+int prefill_timeout_flag(bool clear);
+int decode_timeout_flag(bool clear);
 
 }  // namespace fab

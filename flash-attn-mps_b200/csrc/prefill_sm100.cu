@@ -21,8 +21,6 @@
 // for rows with no visible key) follow the reference's fast kernel
 // flash_attn_mps/kernels/attention_fast.metal:94-597 and its eligibility
 // predicate flash_attn_mps/_attention.py:231-240.
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <mutex>
 
@@ -553,34 +551,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------- host helpers
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
 // [rows, heads, 128] tensor with unit inner stride -> 3-D map, box {64, 1, 128}.
 int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t heads, int64_t s_row,
              int64_t s_head) {
-  auto fn = encode_fn();
-  if (!fn) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)HD, (cuuint64_t)heads, (cuuint64_t)rows};
-  cuuint64_t strides[2] = {(cuuint64_t)(s_head * 2), (cuuint64_t)(s_row * 2)};
-  cuuint32_t box[3] = {64, 1, (cuuint32_t)BM};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dtype == FA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                  const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FA_OK;
+  const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)heads, (uint64_t)rows};
+  const uint64_t strides[2] = {(uint64_t)(s_head * 2), (uint64_t)(s_row * 2)};
+  const uint32_t box[3] = {64, 1, (uint32_t)BM};
+  return encode_tensor_map(map, dtype, 3, ptr, dims, strides, box, true);
 }
 
 bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
@@ -599,8 +576,18 @@ int prefill_sm100_supported(const AttnParams& p) {
     if (v <= 0 || (v * 2) % 16 != 0) return 0;
   if (p.T >= (1 << 30) || p.k_rows <= 0 || p.k_rows >= (1 << 30)) return 0;
   if ((int64_t)((p.max_q + 2 * BM - 1) / (2 * BM)) * p.HQ * p.B >= (1LL << 31)) return 0;
-  if (!encode_fn()) return 0;
+  if (!tensor_map_available()) return 0;
   return 1;
+}
+
+int prefill_timeout_flag(bool clear) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_prefill_timeout, sizeof(int)) != cudaSuccess) return -1;
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(g_prefill_timeout, &zero, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return v;
 }
 
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {

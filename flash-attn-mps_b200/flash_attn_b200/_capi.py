@@ -60,6 +60,7 @@ _P = ctypes.POINTER
 SIGNATURES = {
     "fa_abi_version": [],
     "fa_last_error": [],
+    "fa_pipeline_timeouts": [ctypes.c_int],
     "fa_attention_workspace_size": [_P(AttentionArgs), _P(ctypes.c_size_t)],
     "fa_attention_fwd": [_P(AttentionArgs), ctypes.c_void_p],
     "fa_decode_fwd_noalloc": [_P(AttentionArgs), ctypes.c_void_p],

@@ -103,6 +103,18 @@ int fa_abi_version(void);
 const char* fa_last_error(void);
 
 /*
+ * Pipeline wait time-outs on the current device since the last clear:
+ * bit 0 = the tensor-core prefill kernel, bit 1 = the TMA paged-decode kernel.
+ * Every mbarrier wait in those kernels gives up after a bounded number of
+ * polls, sets its bit and lets the CTA finish, so a stalled pipeline shows
+ * up here instead of hanging the GPU; outputs of the affected launch are then
+ * undefined. clear != 0 resets the bits. Synchronous (reads device memory);
+ * returns -1 on a CUDA error. No counterpart in the reference, whose Metal
+ * kernels have no asynchronous pipelines.
+ */
+int fa_pipeline_timeouts(int clear);
+
+/*
  * Bytes of device workspace fa_attention_fwd needs for these arguments
  * (split-KV partial outputs and LSEs). Host-only; reads no tensor values.
  * Replaces the partial-buffer allocation of flash_attn_mps/_attention.py:244-249
