@@ -198,11 +198,37 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
       // ---------------------------------------------------- TMA producer warp
       // One box = box_tok consecutive tokens of one page (128 bytes of each row
       // per box); boxes of pages past the sequence use page -1, which TMA
-      // treats as out of bounds and fills with zeros.
+      // treats as out of bounds and fills with zeros. The block-table entries
+      // of tile it+1 are fetched right after tile it is issued, so their
+      // latency overlaps the wait for a free slot.
+      constexpr int kBoxesMax = 2 * G::kHalves * (G::kTile / 8);
+      constexpr int kPerLane = (kBoxesMax + 31) / 32;
       const int nbox = G::kTile / box_tok;
       const int total = 2 * G::kHalves * nbox;
+      auto lookup = [&](int it, int (&blk)[kPerLane]) {
+        const int lb = L0 + it * G::kTile;
+#pragma unroll
+        for (int j = 0; j < kPerLane; ++j) {
+          const int i = lane + 32 * j;
+          const int bx = i % nbox;
+          const int logical = lb + bx * box_tok;
+          const int pg = logical >> page_shift;
+          int v = -1;
+          if (i < total && logical - left < len && pg < p.bt_cols) v = __ldg(trow + (int64_t)pg * p.bt1);
+          blk[j] = v;
+        }
+      };
+      if (lane == 0) {
+        sm100::tma_prefetch_desc(&tmk);
+        sm100::tma_prefetch_desc(&tmv);
+      }
+      int next[kPerLane];
+      if (n_tiles > 0) lookup(0, next);
       int issued = 0;
       for (int it = 0; it < n_tiles; ++it) {
+        int cur[kPerLane];
+#pragma unroll
+        for (int j = 0; j < kPerLane; ++j) cur[j] = next[j];
         const int st = it % NST;
         if (it >= NST) {
           const bool ok = sm100::mbar_wait(empty_bar(st), ((it / NST) - 1) & 1, &g_decode_timeout);
@@ -212,20 +238,23 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
         __syncwarp();
         const int lb = L0 + it * G::kTile;
         const uint32_t sbase = smem_u32(smem) + st * G::kStageBytes;
-        for (int i = lane; i < total; i += 32) {
-          const int tensor = i / (G::kHalves * nbox);
-          const int rem = i - tensor * G::kHalves * nbox;
-          const int half = rem / nbox, bx = rem - half * nbox;
-          const int logical = lb + bx * box_tok;
-          const int pg = logical >> page_shift;
-          int blk = -1;
-          if (logical - left < len && pg < p.bt_cols) blk = __ldg(trow + (int64_t)pg * p.bt1);
-          const uint32_t dst = sbase + tensor * (G::kTile * G::kRowBytes) + (uint32_t)((half * G::kTile + bx * box_tok) << 7);
-          sm100::tma_load_4d(dst, tensor ? &tmv : &tmk, full_bar(st), half * (128 / elt), kh,
-                             logical & (p.page - 1), blk);
+#pragma unroll
+        for (int j = 0; j < kPerLane; ++j) {
+          const int i = lane + 32 * j;
+          if (i < total) {
+            const int tensor = i / (G::kHalves * nbox);
+            const int rem = i - tensor * G::kHalves * nbox;
+            const int half = rem / nbox, bx = rem - half * nbox;
+            const int logical = lb + bx * box_tok;
+            const uint32_t dst =
+                sbase + tensor * (G::kTile * G::kRowBytes) + (uint32_t)((half * G::kTile + bx * box_tok) << 7);
+            sm100::tma_load_4d(dst, tensor ? &tmv : &tmk, full_bar(st), half * (128 / elt), kh,
+                               logical & (p.page - 1), cur[j]);
+          }
         }
         __syncwarp();
         issued = it + 1;
+        if (it + 1 < n_tiles) lookup(it + 1, next);
       }
       // Every issued load must land before the CTA leaves.
       for (int it = max(0, issued - NST); it < issued; ++it)
@@ -505,16 +534,18 @@ int page_shift_of(const AttnParams& p) {
   return s;
 }
 
-// CTA shape: warps per CTA (16 tokens each per stage), pipeline stages and the
-// occupancy bound, per K/V storage type.
+// CTA shape: consumer warps per CTA (16 tokens each per stage), pipeline
+// stages and the occupancy bound, per K/V storage type. Measured on B200 with
+// the TMA gather: FP8 4 warps x 3 stages x 4 CTAs/SM (48 KB ring each) beat
+// 8 x 3 x 2 by 2-3% on 64 x 131072-token contexts; bf16 keeps 4 x 3 x 2.
 #ifndef FAB_DECODE_FP8_W
-#define FAB_DECODE_FP8_W 8
+#define FAB_DECODE_FP8_W 4
 #endif
 #ifndef FAB_DECODE_FP8_NST
 #define FAB_DECODE_FP8_NST 3
 #endif
 #ifndef FAB_DECODE_FP8_MINB
-#define FAB_DECODE_FP8_MINB 2
+#define FAB_DECODE_FP8_MINB 4
 #endif
 #ifndef FAB_DECODE_16_W
 #define FAB_DECODE_16_W 4

@@ -1,19 +1,28 @@
 // Varlen / dense prefill on 5th-generation tensor cores (tcgen05 + TMEM + TMA).
 //
-// One CTA computes one 128-row query tile of one (request, query head):
-//   warp 0      TMA producer: Q once, then K/V tiles of 128 keys into a
-//               2-stage ring (128-byte swizzled boxes of 64 head dims).
-//   warp 1      TMEM owner and MMA issuer: S = Q K^T and O += P V as
-//               tcgen05.mma kind::f16 (M=128, N=128, K=16 per instruction),
-//               fp32 accumulators S and O in TMEM (256 columns).
-//   warps 2..5  softmax: each thread owns one query row (its TMEM lane),
-//               loads its S row with tcgen05.ld, applies scale and the
-//               lower-right causal / length masks, runs the online softmax
-//               in the log2 domain, rescales its O row in TMEM when the row
-//               max grows, and writes P (bf16/f16) into a 128-byte swizzled
-//               shared tile that the next MMA reads as its A operand.
-// The MMA warp issues S(j+1) as soon as the softmax warps have read S(j), so
-// the QK^T of the next tile overlaps the exponentials of the current one.
+// Persistent CTAs (one per SM) claim work items -- a pair of 128-row query
+// tiles (A, B) of one (request, query head) -- from an atomic counter,
+// heaviest causal pairs first. Per CTA:
+//   warp 8      TMA producer: Q_A/Q_B once per item, then K(j), V(j), ... as
+//               128-key tiles into an NSLOT-deep ring of 128-byte swizzled
+//               boxes (64 head dims each).
+//   warp 9      TMEM owner and MMA issuer: S = Q K^T from shared memory and
+//               O += P V with P read from tensor memory, as tcgen05.mma
+//               kind::f16 (M=128, N=128, K=16 per instruction); fp32 S_A,
+//               S_B, O_A, O_B in TMEM (4 x 128 columns).
+//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B: each thread
+//               owns one query row (its TMEM lane), loads its S row with
+//               tcgen05.ld, applies scale, softcap and the lower-right
+//               causal / window / length masks, runs the online softmax in
+//               the log2 domain (lazy rescale of its O row in TMEM when the
+//               max grows by more than 2^8), and stores P as packed 16-bit
+//               pairs over the first 64 columns of its own S row
+//               (tcgen05.st). P never touches shared memory, so the tensor
+//               cores' shared-memory operand traffic is Q, K and V only.
+// The MMA warp issues PV(j) of tile A, then QK(j+1) of tile A (which reuses
+// S_A's columns after PV(j) has read P; one thread's tcgen05 MMAs execute in
+// issue order), then the same for tile B, so either warpgroup's exponentials
+// overlap the other tile's MMAs.
 // Every mbarrier wait is bounded; on a timeout the kernel records a flag,
 // drains its own TMA loads and MMAs, frees TMEM and returns.
 //
@@ -35,21 +44,45 @@ using namespace sm100;
 constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;          // keys per tile
 constexpr int HD = 128;          // head dim
-constexpr int NSLOT = 3;         // K/V ring slots (each holds one K or one V tile)
+#ifndef FAB_PREFILL_NSLOT
+#define FAB_PREFILL_NSLOT 5
+#endif
+constexpr int NSLOT = FAB_PREFILL_NSLOT;  // K/V ring slots (each holds one K or one V tile)
 constexpr int kRegion = 128 * 128;            // one 128-row x 64-element box (bytes)
 constexpr int kTileBytes = 2 * kRegion;       // 128 x 128 bf16
-constexpr int kThreads = 320;                 // 2 softmax warpgroups + TMA warp + MMA warp
+constexpr int kThreads = 384;                 // 2 softmax warpgroups + (TMA, MMA, 2 idle) warpgroup
+// Registers: the CTA launches with kLaunchRegs per thread (checked on the host
+// before every launch); the producer warpgroup gives registers back and the
+// softmax warpgroups take them, so that each softmax thread holds its whole
+// 128-column S row. 8 warps x 208 + 4 warps x 88 = 12 warps x 168.
+constexpr int kLaunchRegs = 168;
+#ifndef FAB_PF_SM_REGS
+#define FAB_PF_SM_REGS 208
+#endif
+#ifndef FAB_PF_PR_REGS
+#define FAB_PF_PR_REGS 88
+#endif
+constexpr int kSoftmaxRegs = FAB_PF_SM_REGS;
+constexpr int kProducerRegs = FAB_PF_PR_REGS;
+static_assert(8 * kSoftmaxRegs + 4 * kProducerRegs <= (kThreads / 32) * kLaunchRegs, "register split");
+static_assert(kLaunchRegs * kThreads <= 65536, "launch registers");
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = OFF_QA + kTileBytes;
-constexpr int OFF_PA = OFF_QB + kTileBytes;
-constexpr int OFF_PB = OFF_PA + kTileBytes;
-constexpr int OFF_RING = OFF_PB + kTileBytes;
+constexpr int OFF_RING = OFF_QB + kTileBytes;
 constexpr int OFF_BAR = OFF_RING + NSLOT * kTileBytes;
 constexpr int kSmemBytes = OFF_BAR + 512 + 1024;
 constexpr int NWORK = 4;  // work-id ring slots
 constexpr uint32_t kTmemCols = 512;           // S_A, S_B, O_A, O_B (128 fp32 columns each)
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays <= 2^8 between rescales
+#ifndef FAB_PREFILL_POLY_PAIRS
+#define FAB_PREFILL_POLY_PAIRS 0
+#endif
+// Of every 8 exponential pairs, how many run on the FMA pipe (exp2_poly2)
+// instead of MUFU ex2. Measured on B200 with the single-pass softmax: 0 is
+// fastest (2 and 4 pairs cost 3% and 8%: the softmax is issue-, not
+// MUFU-bound), so the default keeps every exponential on MUFU.
+constexpr int kPolyPairs = FAB_PREFILL_POLY_PAIRS;
 
 enum {
   B_Q = 0, B_QE, B_FULL, B_EMPTY = B_FULL + NSLOT, B_SFA = B_EMPTY + NSLOT, B_SFB, B_PFA, B_PFB, B_ODA, B_ODB,
@@ -100,6 +133,63 @@ __device__ __forceinline__ float rcp(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
   return y;
 }
+// ---- packed f32x2 arithmetic (sm_100 FFMA2 / FADD2) and an FMA-pipe exp2
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair, on the FMA pipe: x = n + f with n = rint(x) (round-to-
+// nearest through the 1.5 * 2^23 shifter), 2^f by a degree-4 minimax
+// polynomial on [-1/2, 1/2] (relative error 5.4e-6, Remez fit with the
+// constant term pinned to 1: flash-attn-mps_b200/csrc/fit_exp2_poly.py), and
+// 2^n added to the exponent field. x is clamped to >= -127 first (NaN kept),
+// which makes 2^(-inf) exactly +0: n = -127, f = 0, p = 1.0 = 127 << 23.
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
+  float x0, x1;
+  f2unpack(x2, x0, x1);
+  x2 = f2pack(max_nan(x0, -127.f), max_nan(x1, -127.f));
+  const uint64_t magic = f2pack(12582912.f, 12582912.f), neg_magic = f2pack(-12582912.f, -12582912.f);
+  const uint64_t t = fadd2(x2, magic);
+  const uint64_t n = fadd2(t, neg_magic);
+  float n0, n1;
+  f2unpack(n, n0, n1);
+  const uint64_t f = fadd2(x2, f2pack(-n0, -n1));
+  uint64_t q = ffma2(f2pack(9.676037356e-03f, 9.676037356e-03f), f, f2pack(5.600578710e-02f, 5.600578710e-02f));
+  q = ffma2(q, f, f2pack(2.402216792e-01f, 2.402216792e-01f));
+  q = ffma2(q, f, f2pack(6.931053400e-01f, 6.931053400e-01f));
+  q = ffma2(q, f, f2pack(1.f, 1.f));
+  float q0, q1, t0, t1;
+  f2unpack(q, q0, q1);
+  f2unpack(t, t0, t1);
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
 // tanh from the identity tanh(y) = 1 - 2 / (e^(2y) + 1): one ex2, one rcp, one
 // FFMA. Absolute error ~1e-6 over the whole range (saturates cleanly to +-1),
 // which a softcap multiplies by the cap.
@@ -225,6 +315,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *holder_ptr;
 
+  if (warp >= 8) {
+  // Producer warpgroup: TMA warp, MMA warp and two idle warps.
+  reg_dealloc<kProducerRegs>();
   if (warp == 8) {
     // ---------------------------------------------------------------- TMA
     uint32_t items = 0, qloads = 0;
@@ -301,13 +394,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
     };
-    auto pv = [&](uint32_t p_off, uint32_t vaddr, uint32_t d, bool acc) {
+    // P (M=128 rows x K=128 keys) is the A operand in TMEM: 16 keys = 8 columns.
+    auto pv = [&](uint32_t p_tmem, uint32_t vaddr, uint32_t d, bool acc) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = sw128_desc(base + p_off + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(vaddr + kk * 2048, kRegion, 1024);
-          mma_f16_ss(d, a, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, p_tmem + kk * 8, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       }
       __syncwarp();
@@ -340,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = warp_wait(bar(B_PFA), pa & 1))) break;
           ++pa;
           tc_fence_after();
-          pv(OFF_PA, slot_addr(iv), tOA, j > it.a0);
+          pv(tSA, slot_addr(iv), tOA, j > it.a0);
           if (j == it.a1 - 1) commit(B_ODA);
         }
         const bool next = t + 1 < it.n_all;
@@ -351,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = warp_wait(bar(B_PFB), pb & 1))) break;
           ++pb;
           tc_fence_after();
-          pv(OFF_PB, slot_addr(iv), tOB, j > it.b0);
+          pv(tSB, slot_addr(iv), tOB, j > it.b0);
           if (j == it.b1 - 1) commit(B_ODB);
         }
         commit(B_EMPTY + iv % NSLOT);
@@ -364,8 +457,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // All MMAs of this CTA must be complete before TMEM is released.
     commit(B_FIN);
     warp_wait(bar(B_FIN), 0);
+  }
   } else {
     // ------------------------------------------------------------ softmax
+    reg_alloc<kSoftmaxRegs>();
     const bool is_b = warp >= 4;
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
@@ -373,7 +468,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = tmem + (is_b ? 128 : 0) + lane_off;
     const uint32_t tO = tmem + (is_b ? 384 : 256) + lane_off;
     const int sf = is_b ? B_SFB : B_SFA, pf = is_b ? B_PFB : B_PFA, od = is_b ? B_ODB : B_ODA;
-    uint8_t* prow = gbase + (is_b ? OFF_PB : OFF_PA) + row * 128;
     uint32_t s_cnt = 0, o_cnt = 0, items = 0, wcnt = 0;
     bool ok = true;
     while (ok) {
@@ -405,25 +499,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int key0 = j * BN;
         const int c_lo = vis.lo - key0, c_hi = vis.hi - key0;  // visible columns of this tile
         const bool need_mask = c_lo > 0 || c_hi < BN - 1;
-        // Pass 1: row max, 64 columns (two TMEM loads in flight) at a time, as 8
-        // independent chains (fp max is exact in any order).
+        // The whole S row in registers: four TMEM loads, one wait.
+        uint32_t r[128];
+        tmem_ld32_at<0>(tS, r);
+        tmem_ld32_at<32>(tS + 32, r);
+        tmem_ld32_at<64>(tS + 64, r);
+        tmem_ld32_at<96>(tS + 96, r);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i < c_lo || i > c_hi) r[i] = __float_as_uint(-INFINITY);
+        }
+        // Row max as 8 independent 3-input max chains (exact in any order).
         float mx8[8];
 #pragma unroll
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = -INFINITY;
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t r[64];
-          tmem_ld32_at<0>(tS + hh * 64, r);
-          tmem_ld32_at<32>(tS + hh * 64 + 32, r);
-          tmem_wait_ld();
-          if (need_mask) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (hh * 64 + i < c_lo || hh * 64 + i > c_hi) r[i] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int i = 0; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(r[i]));
-        }
+        for (int i = 0; i < 128; i += 2)
+          mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         // scale > 0 and tanh is increasing: the max commutes with both.
@@ -433,6 +527,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           factor = m_run == -INFINITY ? 0.f : ex2(m_run - m_tile);
           m_run = m_tile;
         }
+        l_run *= factor;
+        const float msub = m_run == -INFINITY ? 0.f : m_run;
+        // P = 2^(s*scale_log2 - m), masked columns -> 0, packed as 16-bit pairs
+        // into TMEM columns [0, 64) of this row's S, 8 columns per store; the
+        // row sum runs as 8 independent chains (4 packed pairs).
+        uint64_t ls2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
+        const uint64_t sl2x2 = f2pack(sl2, sl2), nmsub2 = f2pack(-msub, -msub);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float p0, p1;
+            const float s0 = __uint_as_float(r[c8 * 16 + 2 * i]), s1 = __uint_as_float(r[c8 * 16 + 2 * i + 1]);
+            if constexpr (SOFTCAP) {
+              p0 = s0 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s0 * cap_in), -msub));
+              p1 = s1 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s1 * cap_in), -msub));
+            } else {
+              const uint64_t x2 = ffma2(f2pack(s0, s1), sl2x2, nmsub2);
+              if (i >= 8 - kPolyPairs) {
+                exp2_poly2(x2, p0, p1);  // FMA pipe
+              } else {
+                float x0, x1;
+                f2unpack(x2, x0, x1);
+                p0 = ex2(x0);  // MUFU
+                p1 = ex2(x1);
+              }
+            }
+            ls2[i & 3] = fadd2(ls2[i & 3], f2pack(p0, p1));
+            pk[i] = pack_p<BF16>(p0, p1);
+          }
+          tmem_st8_at<0>(tS + c8 * 8, pk);
+        }
+        // Lazy O rescale (after the exponentials, while S no longer occupies
+        // registers); PV(j) is issued only after this row's P-ready arrival,
+        // and PV(j-1) completed before S(j) was signalled.
         if (jj > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
@@ -443,47 +575,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
             tmem_st32(tO + c * 32, o);
           }
-          tmem_wait_st();
         }
-        l_run *= factor;
-        const float msub = m_run == -INFINITY ? 0.f : m_run;
-        // Pass 2: P = 2^(s*scale_log2 - m), masked columns -> 0, written to the
-        // swizzled P tile; the row sum runs as 8 independent chains.
-        float ls8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        tmem_wait_st();
+        float ls8[8];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t r[64];
-          tmem_ld32_at<0>(tS + hh * 64, r);
-          tmem_ld32_at<32>(tS + hh * 64 + 32, r);
-          tmem_wait_ld();
-          if (need_mask) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (hh * 64 + i < c_lo || hh * 64 + i > c_hi) r[i] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            uint32_t wv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float p0, p1;
-              const float s0 = __uint_as_float(r[c8 * 8 + 2 * i]), s1 = __uint_as_float(r[c8 * 8 + 2 * i + 1]);
-              if constexpr (SOFTCAP) {
-                p0 = s0 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s0 * cap_in), -msub));
-                p1 = s1 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s1 * cap_in), -msub));
-              } else {
-                p0 = ex2(fmaf(s0, sl2, -msub));
-                p1 = ex2(fmaf(s1, sl2, -msub));
-              }
-              ls8[2 * i] += p0;
-              ls8[2 * i + 1] += p1;
-              wv[i] = pack_p<BF16>(p0, p1);
-            }
-            const int chunk = hh * 8 + c8, region = chunk >> 3, cc = chunk & 7;
-            *reinterpret_cast<uint4*>(prow + region * kRegion + ((cc ^ (row & 7)) << 4)) =
-                make_uint4(wv[0], wv[1], wv[2], wv[3]);
-          }
-        }
+        for (int i = 0; i < 4; ++i) f2unpack(ls2[i], ls8[2 * i], ls8[2 * i + 1]);
         const float lsum = ((ls8[0] + ls8[1]) + (ls8[2] + ls8[3])) + ((ls8[4] + ls8[5]) + (ls8[6] + ls8[7]));
         l_run += lsum;
         if (key0 + BN > it.k_len) {
@@ -500,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               *reinterpret_cast<uint4*>(vrow + kRegion + c * 16) = make_uint4(0, 0, 0, 0);
             }
           }
+          fence_proxy_async_smem();  // generic stores -> the MMA's async-proxy reads
         }
-        fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(bar(pf));
       }
@@ -622,6 +718,14 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
                                 : (cap ? prefill_sm100_kernel<false, true> : prefill_sm100_kernel<false, false>);
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
+  // The warpgroups' setmaxnreg split assumes exactly kLaunchRegs registers per
+  // thread at launch; a build that allocated another count must not run.
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill attributes: %s", cudaGetErrorString(e));
+  if (fa.numRegs != kLaunchRegs)
+    return fail(FA_ERR_CUDA, "prefill kernel built with %d registers per thread, expected %d", fa.numRegs,
+                kLaunchRegs);
   const int64_t n_work = (int64_t)pp.n_pairs * p.HQ * p.B;
   const int grid = (int)std::min<int64_t>(n_work, (int64_t)sm_count());
   if (pp.counter == nullptr) return fail(FA_ERR_INVALID, "prefill needs its workspace counter");
