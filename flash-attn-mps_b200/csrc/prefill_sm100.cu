@@ -45,7 +45,7 @@ constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;          // keys per tile
 constexpr int HD = 128;          // head dim
 #ifndef FAB_PREFILL_NSLOT
-#define FAB_PREFILL_NSLOT 5
+#define FAB_PREFILL_NSLOT 3
 #endif
 constexpr int NSLOT = FAB_PREFILL_NSLOT;  // K/V ring slots (each holds one K or one V tile)
 constexpr int kRegion = 128 * 128;            // one 128-row x 64-element box (bytes)
@@ -69,8 +69,11 @@ static_assert(kLaunchRegs * kThreads <= 65536, "launch registers");
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = OFF_QA + kTileBytes;
 constexpr int OFF_RING = OFF_QB + kTileBytes;
-constexpr int OFF_BAR = OFF_RING + NSLOT * kTileBytes;
-constexpr int kSmemBytes = OFF_BAR + 512 + 1024;
+constexpr int OFF_STAGE = OFF_RING + NSLOT * kTileBytes;  // 8 softmax warps x [2][32 rows][128 B]
+constexpr int kStageWarpBytes = 2 * 32 * 128;
+constexpr int OFF_BAR = OFF_STAGE + 8 * kStageWarpBytes;
+// Barriers, TMEM holder, work-id ring and item ring, then alignment slack.
+constexpr int kSmemBytes = OFF_BAR + 1024 + 1024;
 constexpr int NWORK = 4;  // work-id ring slots
 constexpr uint32_t kTmemCols = 512;           // S_A, S_B, O_A, O_B (128 fp32 columns each)
 constexpr float kLn2 = 0.6931471805599453f;
@@ -78,7 +81,7 @@ constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays <= 2^8 betw
 #ifndef FAB_PREFILL_POLY_PAIRS
 #define FAB_PREFILL_POLY_PAIRS 0
 #endif
-// Of every 8 exponential pairs, how many run on the FMA pipe (exp2_poly2)
+// Of every 8 exponential pairs, how many run on the FMA pipe (Exp2Poly)
 // instead of MUFU ex2. Measured on B200 with the single-pass softmax: 0 is
 // fastest (2 and 4 pairs cost 3% and 8%: the softmax is issue-, not
 // MUFU-bound), so the default keeps every exponential on MUFU.
@@ -163,32 +166,60 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// 2^x for a pair, on the FMA pipe: x = n + f with n = rint(x) (round-to-
-// nearest through the 1.5 * 2^23 shifter), 2^f by a degree-4 minimax
-// polynomial on [-1/2, 1/2] (relative error 5.4e-6, Remez fit with the
-// constant term pinned to 1: flash-attn-mps_b200/csrc/fit_exp2_poly.py), and
-// 2^n added to the exponent field. x is clamped to >= -127 first (NaN kept),
-// which makes 2^(-inf) exactly +0: n = -127, f = 0, p = 1.0 = 127 << 23.
-__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& p0, float& p1) {
-  float x0, x1;
-  f2unpack(x2, x0, x1);
-  x2 = f2pack(max_nan(x0, -127.f), max_nan(x1, -127.f));
-  const uint64_t magic = f2pack(12582912.f, 12582912.f), neg_magic = f2pack(-12582912.f, -12582912.f);
-  const uint64_t t = fadd2(x2, magic);
-  const uint64_t n = fadd2(t, neg_magic);
-  float n0, n1;
-  f2unpack(n, n0, n1);
-  const uint64_t f = fadd2(x2, f2pack(-n0, -n1));
-  uint64_t q = ffma2(f2pack(9.676037356e-03f, 9.676037356e-03f), f, f2pack(5.600578710e-02f, 5.600578710e-02f));
-  q = ffma2(q, f, f2pack(2.402216792e-01f, 2.402216792e-01f));
-  q = ffma2(q, f, f2pack(6.931053400e-01f, 6.931053400e-01f));
-  q = ffma2(q, f, f2pack(1.f, 1.f));
-  float q0, q1, t0, t1;
-  f2unpack(q, q0, q1);
-  f2unpack(t, t0, t1);
-  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
-  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
+
+// 2^x for a pair, on the FMA pipe: x = n + f with n = rint(x) (round-to-
+// nearest through the 1.5 * 2^23 shifter), 2^f by a minimax polynomial on
+// [-1/2, 1/2] (Remez fit with the constant term pinned to 1, relative error
+// 4.3e-4 at degree 3 -- below half a bf16 ulp -- and 5.4e-6 at degree 4 for
+// f16 P; flash-attn-mps_b200/csrc/fit_exp2_poly.py), and 2^n added to the
+// exponent field. x is clamped to >= -127 first (NaN kept), which makes
+// 2^(-inf) exactly +0: n = -127, f = 0, p = 1.0 = 127 << 23. The constant
+// pairs live in registers for the whole tile.
+template <bool BF16>
+struct Exp2Poly {
+  uint64_t magic, c1, c2, c3, c4, one;
+  __device__ __forceinline__ Exp2Poly() {
+    magic = f2pack(12582912.f, 12582912.f);
+    one = f2pack(1.f, 1.f);
+    if constexpr (BF16) {
+      c1 = f2pack(6.957671046e-01f, 6.957671046e-01f);
+      c2 = f2pack(2.420305014e-01f, 2.420305014e-01f);
+      c3 = f2pack(4.169750959e-02f, 4.169750959e-02f);
+      c4 = 0;
+    } else {
+      c1 = f2pack(6.931053400e-01f, 6.931053400e-01f);
+      c2 = f2pack(2.402216792e-01f, 2.402216792e-01f);
+      c3 = f2pack(5.600578710e-02f, 5.600578710e-02f);
+      c4 = f2pack(9.676037356e-03f, 9.676037356e-03f);
+    }
+  }
+  __device__ __forceinline__ void operator()(uint64_t x2, float& p0, float& p1) const {
+    float x0, x1;
+    f2unpack(x2, x0, x1);
+    x2 = f2pack(max_nan(x0, -127.f), max_nan(x1, -127.f));
+    const uint64_t t = fadd2(x2, magic);
+    const uint64_t f = fsub2(x2, fsub2(t, magic));
+    uint64_t q;
+    if constexpr (BF16) {
+      q = ffma2(c3, f, c2);
+    } else {
+      q = ffma2(c4, f, c3);
+      q = ffma2(q, f, c2);
+    }
+    q = ffma2(q, f, c1);
+    q = ffma2(q, f, one);
+    float q0, q1, t0, t1;
+    f2unpack(q, q0, q1);
+    f2unpack(t, t0, t1);
+    p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+  }
+};
 
 // tanh from the identity tanh(y) = 1 - 2 / (e^(2y) + 1): one ex2, one rcp, one
 // FFMA. Absolute error ~1e-6 over the whole range (saturates cleanly to +-1),
@@ -224,12 +255,32 @@ __device__ __forceinline__ void tile_range(int row0, int q_len, int k_len, bool 
 // One work item: a pair of 128-row query tiles of one (request, query head).
 // Items are ordered by pair index descending (the costliest causal tiles
 // first), then head, then request.
+// The TMA warp decodes each claimed item once (including its global reads:
+// sequence offsets, lengths, causal flag, descales, sink) and publishes it in
+// shared memory, so the MMA and softmax warps start an item without any
+// global-memory round trip.
 struct Item {
-  bool valid;
-  int b, h, kh, q_begin, q_len, k_begin, k_len, row_a, row_b;
-  bool causal;
+  int valid, b, h, kh, q_begin, q_len, k_begin, k_len, row_a, row_b, causal;
   int a0, a1, b0, b1, j_first, n_all;
+  float qk_scale, vscale, sink_l2;  // sink_l2: sink logit in log2 units, -inf without one
 };
+constexpr int kItemWords = sizeof(Item) / 4;
+static_assert(sizeof(Item) == 20 * 4, "Item is 20 words");
+
+// Field-wise copies through the shared item ring (no address of a local Item
+// is taken, so the item stays in registers).
+__device__ __forceinline__ void item_store(volatile int* d, const Item& it) {
+  d[0] = it.valid; d[1] = it.b; d[2] = it.h; d[3] = it.kh; d[4] = it.q_begin; d[5] = it.q_len;
+  d[6] = it.k_begin; d[7] = it.k_len; d[8] = it.row_a; d[9] = it.row_b; d[10] = it.causal;
+  d[11] = it.a0; d[12] = it.a1; d[13] = it.b0; d[14] = it.b1; d[15] = it.j_first; d[16] = it.n_all;
+  d[17] = __float_as_int(it.qk_scale); d[18] = __float_as_int(it.vscale); d[19] = __float_as_int(it.sink_l2);
+}
+__device__ __forceinline__ void item_load(const volatile int* d, Item& it) {
+  it.valid = d[0]; it.b = d[1]; it.h = d[2]; it.kh = d[3]; it.q_begin = d[4]; it.q_len = d[5];
+  it.k_begin = d[6]; it.k_len = d[7]; it.row_a = d[8]; it.row_b = d[9]; it.causal = d[10];
+  it.a0 = d[11]; it.a1 = d[12]; it.b0 = d[13]; it.b1 = d[14]; it.j_first = d[15]; it.n_all = d[16];
+  it.qk_scale = __int_as_float(d[17]); it.vscale = __int_as_float(d[18]); it.sink_l2 = __int_as_float(d[19]);
+}
 
 __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   Item it;
@@ -245,11 +296,18 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   it.valid = it.row_a < it.q_len;
   it.n_all = 0;
   it.a0 = it.a1 = it.b0 = it.b1 = it.j_first = 0;
+  it.k_begin = it.k_len = it.kh = it.causal = 0;
+  it.qk_scale = it.vscale = 1.f;
+  it.sink_l2 = -INFINITY;
   if (!it.valid) return it;
   it.k_begin = p.cu_k ? p.cu_k[it.b * p.ck0] : 0;
   it.k_len = p.used ? p.used[it.b * p.u0] : p.cu_k[(it.b + 1) * p.ck0] - it.k_begin;
   it.kh = it.h / (p.HQ / p.HK);
   it.causal = p.causal_b ? p.causal_b[it.b * p.ca0] != 0 : p.causal != 0;
+  it.qk_scale = p.scale * (p.qd ? p.qd[it.b * p.qd0 + it.kh * p.qd1] : 1.f) *
+                (p.kd ? p.kd[it.b * p.kd0 + it.kh * p.kd1] : 1.f);
+  it.vscale = p.vd ? p.vd[it.b * p.vd0 + it.kh * p.vd1] : 1.f;
+  if (p.sinks) it.sink_l2 = load_float(p.sinks, p.sink_t, it.h * p.si0) * 1.4426950408889634f;
   tile_range(it.row_a, it.q_len, it.k_len, it.causal, p.win_l, p.win_r, &it.a0, &it.a1);
   tile_range(it.row_b, it.q_len, it.k_len, it.causal, p.win_l, p.win_r, &it.b0, &it.b1);
   const bool ha = it.a1 > it.a0, hb = it.b1 > it.b0;
@@ -263,7 +321,8 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
 template <bool BF16, bool SOFTCAP>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                         const __grid_constant__ CUtensorMap tv, const PrefillParams p) {
+                         const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                         const PrefillParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -274,12 +333,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t holder = base + OFF_BAR + 8u * B_COUNT;
   volatile uint32_t* holder_ptr = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT);
   volatile int* wring = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * B_COUNT + 16);
+  volatile int* iring = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * B_COUNT + 32);  // [NWORK][20]
   // Work ids flow from the TMA warp (which claims them with an atomic counter,
   // heaviest first) to the MMA warp and the 8 softmax warps through a ring.
-  auto next_work = [&](uint32_t& cnt) -> int {
+  auto next_work = [&](uint32_t& cnt, Item& it) -> int {
     const uint32_t slot = cnt % NWORK;
     if (!warp_wait(base + OFF_BAR + 8u * (B_WFULL + slot), (cnt / NWORK) & 1)) return -2;
     const int w = wring[slot];
+    item_load(iring + slot * kItemWords, it);
     __syncwarp();
     if (lane == 0) mbar_arrive(base + OFF_BAR + 8u * (B_WEMPTY + slot));
     ++cnt;
@@ -340,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (fwd >= NWORK && !(ok = warp_wait(bar(B_WEMPTY + slot), ((fwd / NWORK) - 1) & 1))) break;
         if (lane == 0) {
           wring[slot] = end ? -1 : w;
+          item_store(iring + slot * kItemWords, it);
           mbar_arrive(bar(B_WFULL + slot));
         }
         __syncwarp();
@@ -412,9 +474,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t items = 0, qloads = 0, pa = 0, pb = 0, wcnt = 0;
     bool ok = true;
     while (ok) {
-      const int w = next_work(wcnt);
+      Item it;
+      const int w = next_work(wcnt, it);
       if (w < 0) break;
-      const Item it = make_item(p, w);
       if (it.n_all == 0) continue;
       auto act_a = [&](int j) { return j >= it.a0 && j < it.a1; };
       auto act_b = [&](int j) { return j >= it.b0 && j < it.b1; };
@@ -471,26 +533,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t s_cnt = 0, o_cnt = 0, items = 0, wcnt = 0;
     bool ok = true;
     while (ok) {
-      const int w = next_work(wcnt);
+      Item it;
+      const int w = next_work(wcnt, it);
       if (w < 0) break;
-      const Item it = make_item(p, w);
       const int x0 = is_b ? it.b0 : it.a0, n_x = (is_b ? it.b1 : it.a1) - x0;
       const int q_row = (is_b ? it.row_b : it.row_a) + row;
       const int q_abs = q_row + it.k_len - it.q_len;
       const KeyRange vis = key_range(q_abs, it.k_len, it.causal, p.win_l, p.win_r);
-      const int b = it.b, h = it.h, kh = it.kh;
-      const float qk_scale = p.scale * (p.qd ? p.qd[b * p.qd0 + kh * p.qd1] : 1.f) *
-                             (p.kd ? p.kd[b * p.kd0 + kh * p.kd1] : 1.f);
-      const float vscale = p.vd ? p.vd[b * p.vd0 + kh * p.vd1] : 1.f;
+      const int h = it.h;
+      const float qk_scale = it.qk_scale, vscale = it.vscale;
       const float sl2 = qk_scale * 1.4426950408889634f;     // raw score -> log2 units
       const float cap_l2 = p.softcap * 1.4426950408889634f;  // softcap: cap*log2e*tanh(s*scale/cap)
       const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
       // Running max in log2 units; a sink acts as one extra logit with zero value.
-      float m_run = -INFINITY, l_run = 0.f;
-      if (p.sinks) {
-        m_run = load_float(p.sinks, p.sink_t, h * p.si0) * 1.4426950408889634f;
-        l_run = 1.f;
-      }
+      float m_run = it.sink_l2, l_run = p.sinks ? 1.f : 0.f;
       for (int jj = 0; jj < n_x; ++jj) {
         const int j = x0 + jj;
         if (!(ok = warp_wait(bar(sf), s_cnt & 1))) break;
@@ -536,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
         const uint64_t sl2x2 = f2pack(sl2, sl2), nmsub2 = f2pack(-msub, -msub);
+        const Exp2Poly<BF16> poly;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t pk[8];
@@ -549,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               const uint64_t x2 = ffma2(f2pack(s0, s1), sl2x2, nmsub2);
               if (i >= 8 - kPolyPairs) {
-                exp2_poly2(x2, p0, p1);  // FMA pipe
+                poly(x2, p0, p1);  // FMA pipe
               } else {
                 float x0, x1;
                 f2unpack(x2, x0, x1);
@@ -609,11 +666,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
       }
       // ---------------------------------------------------------- epilogue
+      // O / l in bf16/f16. A warp whose 32 rows all lie inside the sequence
+      // stages them in its own 128-byte-swizzled shared buffer and writes them
+      // with two asynchronous TMA tile stores (coalesced); a warp at the end
+      // of a sequence stores its valid rows directly.
       const bool row_ok = q_row < it.q_len;
       const int64_t t = (int64_t)it.q_begin + q_row;
       const bool have = n_x > 0 && l_run > 0.f;
       const float inv = have ? vscale / l_run : 0.f;
+      const int wrow0 = (is_b ? it.row_b : it.row_a) + sub * 32;
+      const bool staged = wrow0 + 32 <= it.q_len;  // warp-uniform
+      uint8_t* stg = gbase + OFF_STAGE + warp * kStageWarpBytes;
       uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + (t * p.os0 + (int64_t)h * p.os1) * 2;
+      if (staged) {
+        if (lane == 0) bulk_wait_read();  // this warp's previous stores have read the buffer
+        __syncwarp();
+      }
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t r[32];
@@ -621,22 +689,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tO + c * 32, r);
           tmem_wait_ld();
         }
-        if (row_ok) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint32_t wv[4];
+        for (int v = 0; v < 4; ++v) {
+          uint32_t wv[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float a = have ? __uint_as_float(r[v * 8 + 2 * i]) * inv : 0.f;
-              const float bb = have ? __uint_as_float(r[v * 8 + 2 * i + 1]) * inv : 0.f;
-              wv[i] = pack_p<BF16>(a, bb);
-            }
-            *reinterpret_cast<uint4*>(orow + (c * 32 + v * 8) * 2) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          for (int i = 0; i < 4; ++i) {
+            const float a = have ? __uint_as_float(r[v * 8 + 2 * i]) * inv : 0.f;
+            const float bb = have ? __uint_as_float(r[v * 8 + 2 * i + 1]) * inv : 0.f;
+            wv[i] = pack_p<BF16>(a, bb);
           }
+          const uint4 val = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          if (staged) {
+            const int chunk = (c & 1) * 4 + v;
+            *reinterpret_cast<uint4*>(stg + (c >> 1) * 4096 + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = val;
+          } else if (row_ok) {
+            *reinterpret_cast<uint4*>(orow + (c * 32 + v * 8) * 2) = val;
+          }
+        }
+      }
+      if (staged) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const uint32_t sa = smem_addr(stg);
+          tma_store_3d(&to, sa, 0, h, it.q_begin + wrow0);
+          tma_store_3d(&to, sa + 4096, 64, h, it.q_begin + wrow0);
+          bulk_commit();
         }
       }
       if (row_ok) p.lse[(int64_t)h * p.ls0 + t * p.ls1] = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
     }
+    if (lane == 0) bulk_wait_all();  // staged output stores complete before the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -649,10 +732,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------- host helpers
 // [rows, heads, 128] tensor with unit inner stride -> 3-D map, box {64, 1, 128}.
 int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t heads, int64_t s_row,
-             int64_t s_head) {
+             int64_t s_head, int box_rows = BM) {
   const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)heads, (uint64_t)rows};
   const uint64_t strides[2] = {(uint64_t)(s_head * 2), (uint64_t)(s_row * 2)};
-  const uint32_t box[3] = {64, 1, (uint32_t)BM};
+  const uint32_t box[3] = {64, 1, (uint32_t)box_rows};
   return encode_tensor_map(map, dtype, 3, ptr, dims, strides, box, true);
 }
 
@@ -689,11 +772,15 @@ int prefill_timeout_flag(bool clear) {
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   if (p.k_rows <= 0) return fail(FA_ERR_INVALID, "prefill needs packed K/V rows");
   CUtensorMap mq, mk, mv;
+  if (p.T <= 0) return fail(FA_ERR_INVALID, "prefill needs query rows");
   int rc = make_map(&mq, p.q, p.qt, p.T, p.HQ, p.qs0, p.qs1);
   if (rc) return rc;
   rc = make_map(&mk, p.k, p.kt, p.k_rows, p.HK, p.ks1, p.ks2);
   if (rc) return rc;
   rc = make_map(&mv, p.v, p.vt, p.k_rows, p.HK, p.vs1, p.vs2);
+  if (rc) return rc;
+  CUtensorMap mo;  // output tile stores: 32 rows x 64 head dims per box
+  rc = make_map(&mo, p.out, p.ot, p.T, p.HQ, p.os0, p.os1, 32);
   if (rc) return rc;
   PrefillParams pp{};
   pp.out = p.out; pp.os0 = p.os0; pp.os1 = p.os1;
@@ -731,7 +818,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   if (pp.counter == nullptr) return fail(FA_ERR_INVALID, "prefill needs its workspace counter");
   e = cudaMemsetAsync(pp.counter, 0, sizeof(int), stream);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill counter reset: %s", cudaGetErrorString(e));
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, pp);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, mo, pp);
   FAB_LAUNCH_CHECK("prefill launch");
   return FA_OK;
 }
