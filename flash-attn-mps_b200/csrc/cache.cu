@@ -5,9 +5,18 @@
 //   store   kernels/cache.metal:20-39, host _cache.py:166-184
 //   append  kernels/cache.metal:41-56, host _cache.py:198-226
 //   rotate  kernels/cache.metal:58-76, host _cache.py:229-254
-// Each thread moves one 16-byte vector of a (token, head) row when the row is
-// unit-stride and 16-byte aligned, and single elements otherwise; the grid is a
-// multiple of the SM count with a grid-stride loop.
+// store_kvcache: a CTA row of threads covers the (head, 16-byte chunk) pairs of
+// one token, CTA rows take successive tokens (grid-stride over tokens), so the
+// slot lookup and page split happen once per token and a thread's head (and
+// its FP8 reciprocal scale) stays fixed. FP8 quantisation computes x / scale
+// correctly rounded without a division per element: with y = RN(1/scale),
+// q = RN(x*y), r = x - q*scale (exact by FMA), RN(q + r*y) is the correctly
+// rounded quotient (Markstein's theorem for FMA-based division); non-finite
+// quotients take the IEEE division. Pairs are encoded with the packed
+// cvt.rn.satfinite.e4m3x2.f32. append / rotary: one element or 16-byte vector
+// per thread with a grid-stride loop.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace fab {
@@ -22,7 +31,8 @@ struct StoreSide {
   const float* scale;             // FP8 only: [H] or scalar
   int64_t scale_stride;
   int32_t H, D, P;
-  int64_t units;                  // T*H*(D/VEC)
+  int32_t pshift;                 // log2(P) when P is a power of two, else -1
+  int64_t tokens;
 };
 
 struct StoreArgs {
@@ -34,47 +44,141 @@ struct StoreArgs {
 
 template <typename T> struct Vec16 { static constexpr int N = 16 / sizeof(T); };
 
+// RN(x / s) for E4M3 encoding, given y = RN(1/s), with no division and no
+// per-element branch: q = x*y is clamped to +-1e4 (every quotient beyond
+// +-464 saturates to the same +-448 code; NaN propagates through the
+// NaN-keeping min/max), Markstein's FMA correction then yields the correctly
+// rounded quotient, and the sign of q is restored for an exact -0 quotient.
+__device__ __forceinline__ float quotient_for_e4m3(float x, float s, float y) {
+  float q = x * y;
+  asm("max.NaN.f32 %0, %0, 0fC61C4000;\n\tmin.NaN.f32 %0, %0, 0f461C4000;" : "+f"(q));  // -1e4, 1e4
+  const float r = fmaf(-q, s, x);
+  return copysignf(fmaf(r, y, q), q);
+}
+
+// Two values -> two E4M3 codes (saturating round-to-nearest-even; the NaNs
+// that reach here are the GPU's canonical positive NaN, encoded 0x7F).
+__device__ __forceinline__ uint32_t e4m3x2_sat(float a, float b) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+}
+
+// A 16-byte vector of VEC inputs as float32.
+template <typename T>
+__device__ __forceinline__ void vec_to_f32(const uint4& raw, float (&f)[16 / sizeof(T)]) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(w[i]);
+  } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = v.x;
+      f[2 * i + 1] = v.y;
+    }
+  }
+}
+
+__device__ __forceinline__ int64_t page_of(int64_t slot, int P, int pshift) {
+  if (pshift >= 0) return slot >> pshift;
+  if (slot < 0x7fffffff) return (int64_t)((uint32_t)slot / (uint32_t)P);
+  return slot / P;
+}
+
+// One 16-byte input vector (already loaded) of one (token, head) row.
+template <typename T, bool FP8>
+__device__ __forceinline__ void store_vector16(const StoreSide& s, const uint4& raw, int64_t dst, float scale,
+                                               float rscale) {
+  constexpr int VEC = 16 / sizeof(T);
+  if constexpr (!FP8) {
+    *reinterpret_cast<uint4*>(reinterpret_cast<T*>(s.cache) + dst) = raw;
+  } else {
+    uint8_t* cache = reinterpret_cast<uint8_t*>(s.cache);
+    float f[VEC];
+    vec_to_f32<T>(raw, f);
+    uint32_t codes[VEC / 4];
+#pragma unroll
+    for (int i = 0; i < VEC / 4; ++i)
+      codes[i] = e4m3x2_sat(quotient_for_e4m3(f[4 * i], scale, rscale), quotient_for_e4m3(f[4 * i + 1], scale, rscale)) |
+                 (e4m3x2_sat(quotient_for_e4m3(f[4 * i + 2], scale, rscale),
+                             quotient_for_e4m3(f[4 * i + 3], scale, rscale)) << 16);
+    if constexpr (VEC == 8) {
+      *reinterpret_cast<uint2*>(cache + dst) = make_uint2(codes[0], codes[1]);
+    } else {
+      *reinterpret_cast<uint32_t*>(cache + dst) = codes[0];
+    }
+  }
+}
+
+// Element-wise path (strided or unaligned rows).
+template <typename T, bool FP8, int VEC>
+__device__ __forceinline__ void store_scalar(const StoreSide& s, int64_t src, int64_t dst, float scale) {
+  const T* x = reinterpret_cast<const T*>(s.x);
+  for (int i = 0; i < VEC; ++i) {
+    if constexpr (FP8)
+      reinterpret_cast<uint8_t*>(s.cache)[dst + i * s.cs3] = float_to_e4m3_sat(__fdiv_rn((float)x[src + i * s.xs2], scale));
+    else
+      reinterpret_cast<T*>(s.cache)[dst + i * s.cs3] = x[src + i * s.xs2];
+  }
+}
+
+// blockDim.x threads cover the H * D/VEC vectors of a token (looping when
+// there are more), blockDim.y token rows per CTA; each thread carries kTokU
+// tokens per step so that kTokU slot loads and then kTokU vector loads are in
+// flight before the first conversion (the kernel is otherwise latency-bound).
+constexpr int kTokU = 4;
+
 template <typename T, bool FP8, int VEC>
 __global__ void __launch_bounds__(256) store_kernel(StoreArgs a) {
   const StoreSide& s = a.side[blockIdx.y];
   if (s.x == nullptr) return;
   const int chunks = s.D / VEC;
-  const int64_t step = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < s.units; u += step) {
-    const int c = (int)(u % chunks);
-    const int64_t r = u / chunks;
-    const int h = (int)(r % s.H);
-    const int64_t t = r / s.H;
-    const int64_t slot = load_index(a.slots, a.slot_dtype, t * a.slot_stride);
-    if (slot < 0 || slot >= s.capacity) continue;
-    const int64_t block = slot / s.P, off = slot - block * s.P;
-    const int64_t src = t * s.xs0 + h * s.xs1 + (int64_t)c * VEC * s.xs2;
-    const int64_t dst = block * s.cs0 + off * s.cs1 + h * s.cs2 + (int64_t)c * VEC * s.cs3;
-    const T* x = reinterpret_cast<const T*>(s.x);
-    if constexpr (!FP8) {
-      T* cache = reinterpret_cast<T*>(s.cache);
-      if constexpr (VEC * sizeof(T) == 16) {
-        *reinterpret_cast<uint4*>(cache + dst) = __ldg(reinterpret_cast<const uint4*>(x + src));
-      } else {
-        for (int i = 0; i < VEC; ++i) cache[dst + i * s.cs3] = x[src + i * s.xs2];
-      }
-    } else {
-      uint8_t* cache = reinterpret_cast<uint8_t*>(s.cache);
-      const float scale = s.scale ? s.scale[h * s.scale_stride] : 1.0f;
-      if constexpr (VEC * sizeof(T) == 16) {
-        uint4 raw = __ldg(reinterpret_cast<const uint4*>(x + src));
-        const T* v = reinterpret_cast<const T*>(&raw);
-        uint8_t codes[VEC];
+  const int per_token = s.H * chunks;
+  const int64_t rows = (int64_t)gridDim.x * blockDim.y;  // token rows in flight across the grid
+  const int64_t tstep = rows * kTokU;
+  for (int64_t t0 = (int64_t)blockIdx.x * blockDim.y + threadIdx.y; t0 < s.tokens; t0 += tstep) {
+    int64_t dtok[kTokU], stok[kTokU];
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) codes[i] = float_to_e4m3_sat(__fdiv_rn((float)v[i], scale));
-        if constexpr (VEC == 8) {
-          *reinterpret_cast<uint2*>(cache + dst) = *reinterpret_cast<const uint2*>(codes);
-        } else {
-          *reinterpret_cast<uint32_t*>(cache + dst) = *reinterpret_cast<const uint32_t*>(codes);
-        }
+    for (int u = 0; u < kTokU; ++u) {
+      const int64_t t = t0 + u * rows;
+      int64_t slot = -1;
+      if (t < s.tokens) slot = load_index(a.slots, a.slot_dtype, t * a.slot_stride);
+      if (slot < 0 || slot >= s.capacity) {
+        dtok[u] = -1;
       } else {
-        for (int i = 0; i < VEC; ++i)
-          cache[dst + i * s.cs3] = float_to_e4m3_sat(__fdiv_rn((float)x[src + i * s.xs2], scale));
+        const int64_t block = page_of(slot, s.P, s.pshift), off = slot - block * s.P;
+        dtok[u] = block * s.cs0 + off * s.cs1;
+      }
+      stok[u] = t * s.xs0;
+    }
+    for (int i = threadIdx.x; i < per_token; i += blockDim.x) {
+      const int h = i / chunks, c = i - h * chunks;
+      float scale = 1.f, rscale = 1.f;
+      if constexpr (FP8) {
+        if (s.scale) {
+          scale = __ldg(s.scale + h * s.scale_stride);
+          rscale = __frcp_rn(scale);
+        }
+      }
+      const int64_t soff = h * s.xs1 + (int64_t)c * VEC * s.xs2, doff = h * s.cs2 + (int64_t)c * VEC * s.cs3;
+      if constexpr (VEC * sizeof(T) == 16) {
+        uint4 raw[kTokU];
+#pragma unroll
+        for (int u = 0; u < kTokU; ++u)
+          if (dtok[u] >= 0) raw[u] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(s.x) + stok[u] + soff));
+#pragma unroll
+        for (int u = 0; u < kTokU; ++u)
+          if (dtok[u] >= 0) store_vector16<T, FP8>(s, raw[u], dtok[u] + doff, scale, rscale);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kTokU; ++u)
+          if (dtok[u] >= 0) store_scalar<T, FP8, VEC>(s, stok[u] + soff, dtok[u] + doff, scale);
       }
     }
   }
@@ -122,22 +226,27 @@ int prepare_side(const fa_tensor* x, const fa_tensor* cache, const fa_tensor* sc
          (s->xs0 * esz) % 16 == 0 && (s->xs1 * esz) % 16 == 0 &&
          (s->cs0 * (*fp8 ? 1 : esz)) % out_bytes == 0 && (s->cs1 * (*fp8 ? 1 : esz)) % out_bytes == 0 &&
          (s->cs2 * (*fp8 ? 1 : esz)) % out_bytes == 0;
-  s->units = tokens * s->H * (int64_t)(*vec ? s->D / v : s->D);
+  s->tokens = tokens;
+  s->pshift = -1;
+  for (int k = 0; k < 31; ++k)
+    if ((1 << k) == s->P) s->pshift = k;
   return FA_OK;
 }
 
 template <typename T, bool FP8>
 void launch_store(const StoreArgs& a, bool vec, int sides, cudaStream_t stream) {
-  int64_t units = a.side[0].x ? a.side[0].units : 0;
-  if (sides > 1 && a.side[1].x) units = units > a.side[1].units ? units : a.side[1].units;
-  const int threads = 256;
-  int64_t blocks = (units + threads - 1) / threads;
+  const StoreSide& s0 = a.side[0].x ? a.side[0] : a.side[1];
+  const int per_token = s0.H * (vec ? s0.D / Vec16<T>::N : s0.D);  // both sides share H, D
+  int bx = (per_token + 31) / 32 * 32;
+  if (bx > 256) bx = 256;
+  const int by = 256 / bx;
+  int64_t blocks = (s0.tokens + (int64_t)by * kTokU - 1) / ((int64_t)by * kTokU);
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  dim3 grid((unsigned)blocks, (unsigned)sides);
-  if (vec) store_kernel<T, FP8, Vec16<T>::N><<<grid, threads, 0, stream>>>(a);
-  else store_kernel<T, FP8, 1><<<grid, threads, 0, stream>>>(a);
+  dim3 grid((unsigned)blocks, (unsigned)sides), block((unsigned)bx, (unsigned)by);
+  if (vec) store_kernel<T, FP8, Vec16<T>::N><<<grid, block, 0, stream>>>(a);
+  else store_kernel<T, FP8, 1><<<grid, block, 0, stream>>>(a);
 }
 
 int dispatch_store(const StoreArgs& a, int dtype, bool fp8, bool vec, int sides, cudaStream_t st) {
@@ -310,11 +419,11 @@ extern "C" int fa_store_kvcache(const fa_tensor* key, const fa_tensor* value,
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const bool have0 = a.side[0].x != nullptr, have1 = a.side[1].x != nullptr;
   if (have0 && have1 && dt[0] == dt[1] && fp8[0] == fp8[1] && vec[0] == vec[1]) {
-    if (a.side[0].units == 0 && a.side[1].units == 0) return FA_OK;
+    if ((int64_t)a.side[0].H * a.side[0].D == 0 && (int64_t)a.side[1].H * a.side[1].D == 0) return FA_OK;
     return dispatch_store(a, dt[0], fp8[0], vec[0], 2, st);
   }
   for (int i = 0; i < 2; ++i) {
-    if (a.side[i].x == nullptr || a.side[i].units == 0) continue;
+    if (a.side[i].x == nullptr || (int64_t)a.side[i].H * a.side[i].D == 0) continue;
     StoreArgs one = a;
     one.side[0] = a.side[i];
     rc = dispatch_store(one, dt[i], fp8[i], vec[i], 1, st);

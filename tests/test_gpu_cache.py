@@ -68,15 +68,18 @@ def test_fp8_rne_saturation_and_scales(device):
 
 @pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_fp8_exhaustive_against_torch_cast(device, src_dtype):
-    # Every bf16 bit pattern (and its f16/f32 value) under four per-head scales,
+    # Every bf16 bit pattern (and its f16/f32 value) under eight per-head scales,
     # vectorised 16-byte path: bit-exact with torch's cast of the clamped quotient.
     bits = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).float()
     bits = bits[torch.isfinite(bits)]
     x = bits.to(src_dtype)
     x = x[torch.isfinite(x)]
-    heads = 4
+    # Powers of two plus scales whose quotients are inexact (the division must
+    # still round exactly like x / scale in float32).
+    scale = torch.tensor([1.0, 0.5, 2.0, 3.0 / 448.0, 0.1, 1.0 / 3.0, 1.7 / 448.0, 0.0123],
+                         dtype=torch.float32)
+    heads = scale.numel()
     rows = x.reshape(-1, 1, 1).expand(-1, heads, 8).contiguous()
-    scale = torch.tensor([1.0, 0.5, 2.0, 3.0 / 448.0], dtype=torch.float32)
     cache = torch.empty((rows.shape[0], 1, heads, 8), dtype=torch.float8_e4m3fn, device=device)
     store_kvcache(rows.to(device), rows.to(device), cache, cache,
                   torch.arange(rows.shape[0], device=device), k_scale=scale.to(device),
@@ -86,6 +89,21 @@ def test_fp8_exhaustive_against_torch_cast(device, src_dtype):
     # The oracle's encoder agrees with both.
     codes = oracle.e4m3_encode((rows.float() / scale[None, :, None]).numpy())
     np.testing.assert_array_equal(codes, expected.view(torch.uint8).numpy())
+
+
+def test_fp8_random_float32_quotients_round_exactly(device):
+    # Full-mantissa float32 inputs over a wide exponent range and inexact
+    # per-head scales: codes equal torch's cast of the IEEE quotient.
+    g = torch.Generator().manual_seed(9)
+    tokens, heads, dim = 2048, 8, 64
+    x = torch.randn(tokens, heads, dim, generator=g) * torch.exp2(torch.randint(-12, 12, (tokens, heads, dim),
+                                                                                  generator=g).float())
+    scale = torch.rand(heads, generator=g) * 0.9 + 0.05
+    cache = torch.empty((tokens, 1, heads, dim), dtype=torch.float8_e4m3fn, device=device)
+    store_kvcache(x.to(device), x.to(device), cache, cache, torch.arange(tokens, device=device),
+                  k_scale=scale.to(device), v_scale=scale.to(device))
+    expected = (x / scale[None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(cache.view(torch.uint8).cpu()[:, 0], expected.view(torch.uint8))
 
 
 def test_store_matches_oracle_at_bench_shape_sample(device):
