@@ -150,6 +150,11 @@ __device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -180,13 +185,13 @@ __device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
 // exponent field. x is clamped to >= -127 first (NaN kept), which makes
 // 2^(-inf) exactly +0: n = -127, f = 0, p = 1.0 = 127 << 23. The constant
 // pairs live in registers for the whole tile.
-template <bool BF16>
+template <bool DEG3>
 struct Exp2Poly {
   uint64_t magic, c1, c2, c3, c4, one;
   __device__ __forceinline__ Exp2Poly() {
     magic = f2pack(12582912.f, 12582912.f);
     one = f2pack(1.f, 1.f);
-    if constexpr (BF16) {
+    if constexpr (DEG3) {
       c1 = f2pack(6.957671046e-01f, 6.957671046e-01f);
       c2 = f2pack(2.420305014e-01f, 2.420305014e-01f);
       c3 = f2pack(4.169750959e-02f, 4.169750959e-02f);
@@ -201,11 +206,14 @@ struct Exp2Poly {
   __device__ __forceinline__ void operator()(uint64_t x2, float& p0, float& p1) const {
     float x0, x1;
     f2unpack(x2, x0, x1);
-    x2 = f2pack(max_nan(x0, -127.f), max_nan(x1, -127.f));
+    in_range(f2pack(max_nan(x0, -127.f), max_nan(x1, -127.f)), p0, p1);
+  }
+  // x already within [-126, 126].
+  __device__ __forceinline__ void in_range(uint64_t x2, float& p0, float& p1) const {
     const uint64_t t = fadd2(x2, magic);
     const uint64_t f = fsub2(x2, fsub2(t, magic));
     uint64_t q;
-    if constexpr (BF16) {
+    if constexpr (DEG3) {
       q = ffma2(c3, f, c2);
     } else {
       q = ffma2(c4, f, c3);
@@ -592,7 +600,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
         const uint64_t sl2x2 = f2pack(sl2, sl2), nmsub2 = f2pack(-msub, -msub);
-        const Exp2Poly<BF16> poly;
+        // softcap constants: e^(2y) = 2^(s * cap_in * 2 log2e)
+        const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
+        const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
+        const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
+        const Exp2Poly<BF16> poly;  // degree 3 for bf16 P, 4 for f16 P
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint32_t pk[8];
@@ -601,8 +613,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             float p0, p1;
             const float s0 = __uint_as_float(r[c8 * 16 + 2 * i]), s1 = __uint_as_float(r[c8 * 16 + 2 * i + 1]);
             if constexpr (SOFTCAP) {
-              p0 = s0 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s0 * cap_in), -msub));
-              p1 = s1 == -INFINITY ? 0.f : ex2(fmaf(cap_l2, tanh_id(s1 * cap_in), -msub));
+              // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1):
+              // e^(2y) on the FMA pipe (degree-4 polynomial, argument clamped
+              // to +-64 where tanh is +-1 in fp32), one MUFU rcp, one MUFU ex2.
+              float u0, u1;
+              f2unpack(fmul2(f2pack(s0, s1), tanh_k2), u0, u1);
+              float e0, e1;
+              tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
+              float d0, d1;
+              f2unpack(fadd2(f2pack(e0, e1), one2), d0, d1);
+              const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
+              float l0, l1;
+              f2unpack(ffma2(t2, cap_l2x2, nmsub2), l0, l1);
+              p0 = s0 == -INFINITY ? 0.f : ex2(l0);
+              p1 = s1 == -INFINITY ? 0.f : ex2(l1);
             } else {
               const uint64_t x2 = ffma2(f2pack(s0, s1), sl2x2, nmsub2);
               if (i >= 8 - kPolyPairs) {
