@@ -106,6 +106,8 @@ struct PrefillParams {
   const float* kd; int64_t kd0, kd1;
   const float* vd; int64_t vd0, vd1;
   int* counter;                           // work counter, zero at launch
+  const int32_t* table; int64_t bt0, bt1;  // paged K/V: block_table [B, bt_cols] (null for packed K/V)
+  int32_t bt_cols, page_shift, box_rows;   // page = 1 << page_shift tokens, box_rows = min(page, 128)
   int32_t B, HQ, HK, n_pairs, causal, win_l, win_r;
   float scale, softcap;
 };
@@ -430,13 +432,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < 2 * it.n_all; ++i) {  // K(j), V(j), K(j+1), ...
         const uint32_t slot = items % NSLOT;
         if (items >= NSLOT && !(ok = warp_wait(bar(B_EMPTY + slot), ((items / NSLOT) - 1) & 1))) break;
-        if (lane == 0) {
-          const CUtensorMap* map = (i & 1) ? &tv : &tk;
-          const int row = it.k_begin + (it.j_first + (i >> 1)) * BN;
-          const uint32_t dst = base + OFF_RING + slot * kTileBytes;
-          mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
-          tma_load_3d(dst, map, bar(B_FULL + slot), 0, it.kh, row);
-          tma_load_3d(dst + kRegion, map, bar(B_FULL + slot), 64, it.kh, row);
+        const CUtensorMap* map = (i & 1) ? &tv : &tk;
+        const uint32_t dst = base + OFF_RING + slot * kTileBytes;
+        if (p.table == nullptr) {
+          if (lane == 0) {
+            const int row = it.k_begin + (it.j_first + (i >> 1)) * BN;
+            mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
+            tma_load_3d(dst, map, bar(B_FULL + slot), 0, it.kh, row);
+            tma_load_3d(dst + kRegion, map, bar(B_FULL + slot), 64, it.kh, row);
+          }
+        } else {
+          // Paged K/V: the tile's 128 keys arrive as page boxes (box_rows
+          // tokens x 64 head dims each, one lane per box) through
+          // block_table; pages past the sequence or the table use page -1,
+          // which TMA fills with zeros.
+          const int nb = BN / p.box_rows;
+          const int key0 = (it.j_first + (i >> 1)) * BN;
+          if (lane == 0) mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
+          __syncwarp();
+          if (lane < 2 * nb) {
+            const int half = lane / nb, c = lane - half * nb;
+            const int pos = key0 + c * p.box_rows;
+            const int pg = pos >> p.page_shift;
+            int blk = -1;
+            if (pos < it.k_len && pg < p.bt_cols) blk = __ldg(p.table + (int64_t)it.b * p.bt0 + (int64_t)pg * p.bt1);
+            tma_load_4d(dst + half * kRegion + c * p.box_rows * 128, map, bar(B_FULL + slot), half * 64, it.kh,
+                        pos & ((1 << p.page_shift) - 1), blk);
+          }
+          __syncwarp();
         }
         ++items;
       }
@@ -754,6 +777,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------- host helpers
+// Paged [pages, page, heads, 128] cache -> 4-D map (dims, heads, token in page,
+// page), box {64, 1, box_rows, 1}.
+int make_page_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads, int64_t page, int64_t pages,
+                  int64_t s_page, int64_t s_tok, int64_t s_head, int box_rows) {
+  const uint64_t dims[4] = {(uint64_t)HD, (uint64_t)heads, (uint64_t)page, (uint64_t)pages};
+  const uint64_t strides[3] = {(uint64_t)(s_head * 2), (uint64_t)(s_tok * 2), (uint64_t)(s_page * 2)};
+  const uint32_t box[4] = {64, 1, (uint32_t)box_rows, 1};
+  return encode_tensor_map(map, dtype, 4, ptr, dims, strides, box, true);
+}
 // [rows, heads, 128] tensor with unit inner stride -> 3-D map, box {64, 1, 128}.
 int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t heads, int64_t s_row,
              int64_t s_head, int box_rows = BM) {
@@ -769,7 +801,16 @@ bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
 int prefill_sm100_supported(const AttnParams& p) {
   if (!(p.qt == FA_BF16 || p.qt == FA_F16) || p.kt != p.qt || p.vt != p.qt || p.ot != p.qt) return 0;
-  if (p.DQ != HD || p.DV != HD || p.paged) return 0;
+  if (p.DQ != HD || p.DV != HD) return 0;
+  if (p.paged) {
+    // Paged K/V: power-of-two pages of >= 8 tokens (whole 1024-byte swizzle
+    // atoms per box), a page stride TMA can address.
+    if (p.page < 8 || (p.page & (p.page - 1)) || p.k_pages <= 0 || p.k_pages >= (1LL << 31)) return 0;
+    if (p.bt_cols <= 0 || p.bt_cols >= (1LL << 31)) return 0;
+    const int64_t ps[2] = {p.ks0, p.vs0};
+    for (int64_t v : ps)
+      if (v <= 0 || (v * 2) % 16 != 0) return 0;
+  }
   if (p.alibi || p.mask || p.leftpad) return 0;
   if (p.sinks && !(p.sink_t == FA_F32 || p.sink_t == FA_F16 || p.sink_t == FA_BF16)) return 0;
   if (p.qs2 != 1 || p.ks3 != 1 || p.vs3 != 1 || p.os2 != 1) return 0;
@@ -777,7 +818,8 @@ int prefill_sm100_supported(const AttnParams& p) {
   const int64_t s[8] = {p.qs0, p.qs1, p.ks1, p.ks2, p.vs1, p.vs2, p.os0, p.os1};
   for (int64_t v : s)
     if (v <= 0 || (v * 2) % 16 != 0) return 0;
-  if (p.T >= (1 << 30) || p.k_rows <= 0 || p.k_rows >= (1 << 30)) return 0;
+  if (p.T >= (1 << 30)) return 0;
+  if (!p.paged && (p.k_rows <= 0 || p.k_rows >= (1 << 30))) return 0;
   if ((int64_t)((p.max_q + 2 * BM - 1) / (2 * BM)) * p.HQ * p.B >= (1LL << 31)) return 0;
   if (!tensor_map_available()) return 0;
   return 1;
@@ -794,15 +836,25 @@ int prefill_timeout_flag(bool clear) {
 }
 
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
-  if (p.k_rows <= 0) return fail(FA_ERR_INVALID, "prefill needs packed K/V rows");
   CUtensorMap mq, mk, mv;
   if (p.T <= 0) return fail(FA_ERR_INVALID, "prefill needs query rows");
   int rc = make_map(&mq, p.q, p.qt, p.T, p.HQ, p.qs0, p.qs1);
   if (rc) return rc;
-  rc = make_map(&mk, p.k, p.kt, p.k_rows, p.HK, p.ks1, p.ks2);
-  if (rc) return rc;
-  rc = make_map(&mv, p.v, p.vt, p.k_rows, p.HK, p.vs1, p.vs2);
-  if (rc) return rc;
+  int page_shift = 0, box_rows = 0;
+  if (p.paged) {
+    while ((1 << page_shift) < p.page) ++page_shift;
+    box_rows = p.page < BN ? p.page : BN;
+    rc = make_page_map(&mk, p.k, p.kt, p.HK, p.page, p.k_pages, p.ks0, p.ks1, p.ks2, box_rows);
+    if (rc) return rc;
+    rc = make_page_map(&mv, p.v, p.vt, p.HK, p.page, p.k_pages, p.vs0, p.vs1, p.vs2, box_rows);
+    if (rc) return rc;
+  } else {
+    if (p.k_rows <= 0) return fail(FA_ERR_INVALID, "prefill needs packed K/V rows");
+    rc = make_map(&mk, p.k, p.kt, p.k_rows, p.HK, p.ks1, p.ks2);
+    if (rc) return rc;
+    rc = make_map(&mv, p.v, p.vt, p.k_rows, p.HK, p.vs1, p.vs2);
+    if (rc) return rc;
+  }
   CUtensorMap mo;  // output tile stores: 32 rows x 64 head dims per box
   rc = make_map(&mo, p.out, p.ot, p.T, p.HQ, p.os0, p.os1, 32);
   if (rc) return rc;
@@ -814,6 +866,10 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.used = p.used; pp.u0 = p.u0;
   pp.B = p.B; pp.HQ = p.HQ; pp.HK = p.HK;
   pp.counter = reinterpret_cast<int*>(p.scratch);
+  if (p.paged) {
+    pp.table = p.table; pp.bt0 = p.bt0; pp.bt1 = p.bt1;
+    pp.bt_cols = (int32_t)p.bt_cols; pp.page_shift = page_shift; pp.box_rows = box_rows;
+  }
   pp.n_pairs = (p.max_q + 2 * BM - 1) / (2 * BM);
   pp.causal = p.causal;
   pp.causal_b = p.dynamic ? p.causal_b : nullptr; pp.ca0 = p.ca0;

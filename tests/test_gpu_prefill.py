@@ -153,3 +153,64 @@ def test_dynamic_causal_and_descales_on_tensor_core_path(device):
     ref, refl = reference(q, k, v, cq, ck, causal=dyn, q_descale=qs, k_descale=ks, v_descale=vs)
     assert_attention_close(out, ref)
     assert_lse_close(lse, refl)
+
+
+def _paged_kv(device, dtype, klens, page, hk, seed, columns_extra=1):
+    """K/V in a paged cache [pages, page, hk, 128] with NaN-poisoned slots past
+    each sequence and -1 table entries for pages wholly past it."""
+    g = torch.Generator().manual_seed(seed)
+    B = len(klens)
+    columns = max((n + page - 1) // page for n in klens) + columns_extra
+    n_pages = B * columns + 1
+    table = torch.randperm(n_pages, generator=g)[:B * columns].int().reshape(B, columns)
+    raw = [torch.randn(n_pages, page, hk, 128, generator=g) for _ in range(2)]
+    for b, n in enumerate(klens):
+        for col in range(columns):
+            lo = col * page
+            for pos in range(max(lo, n), lo + page):
+                for r in raw:
+                    r[int(table[b, col]), pos - lo] = float("nan")
+            if lo >= n:
+                table[b, col] = -1
+    k, v = (r.to(dtype).to(device) for r in raw)
+    return k, v, table.to(device)
+
+
+@pytest.mark.parametrize("page", [16, 64, 256])
+@pytest.mark.parametrize("causal", [True, False])
+def test_paged_prefill_chunks_over_cached_prefix(device, page, causal):
+    # Chunked prefill: new query tokens attend over a paged cache holding the
+    # prefix plus themselves (q_len <= k_len, lower-right causal).
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_attention
+    qlens, klens = [1, 130, 300, 64], [700, 130, 1025, 2000]
+    k, v, table = _paged_kv(device, torch.bfloat16, klens, page, 4, seed=page)
+    g = torch.Generator().manual_seed(31)
+    q = torch.randn(sum(qlens), 16, 128, generator=g).to(torch.bfloat16).to(device)
+    cq = cu(qlens, device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    out, lse = vllm_attention(q, k, v, max(qlens), cq, max(klens), seqused_k=used, block_table=table,
+                              causal=causal, return_softmax_lse=True)
+    ref, refl = reference(q, k, v, cq, used_k=used, block_table=table, causal=causal)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_paged_prefill_features(device, dtype):
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_attention
+    qlens, klens = [200, 513, 33], [200, 900, 400]
+    k, v, table = _paged_kv(device, dtype, klens, 32, 2, seed=8)
+    g = torch.Generator().manual_seed(32)
+    q = (torch.randn(sum(qlens), 8, 128, generator=g) * 2).to(dtype).to(device)
+    cq = cu(qlens, device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    sinks = torch.linspace(-1, 1, 8, device=device)
+    kd = torch.tensor([[.5, 1.25]], device=device).expand(3, 2)
+    vd = torch.tensor([[2., .75]], device=device).expand(3, 2)
+    out, lse = vllm_attention(q, k, v, max(qlens), cq, max(klens), seqused_k=used, block_table=table,
+                              causal=True, window_size=[255, 0], softcap=20.0, s_aux=sinks,
+                              k_descale=kd, v_descale=vd, return_softmax_lse=True)
+    ref, refl = reference(q, k, v, cq, used_k=used, block_table=table, causal=True, window=(255, 0),
+                          softcap=20.0, sinks=sinks, k_descale=kd, v_descale=vd)
+    assert_attention_close(out, ref, dtype)
+    assert_lse_close(lse, refl)
