@@ -31,6 +31,7 @@
 // flash_attn_mps/kernels/attention_fast.metal:94-597 and its eligibility
 // predicate flash_attn_mps/_attention.py:231-240.
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -43,7 +44,7 @@ using namespace sm100;
 
 constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
 constexpr int BN = 128;          // keys per tile
-constexpr int HD = 128;          // head dim
+constexpr int HD = 128;          // largest head dim (shared-memory slots are sized for it)
 #ifndef FAB_PREFILL_NSLOT
 #define FAB_PREFILL_NSLOT 3
 #endif
@@ -328,11 +329,15 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   return it;
 }
 
-template <bool BF16, bool SOFTCAP>
+// HDIM: head dim (64 or 128) = number of 64-element swizzle regions x 64.
+template <bool BF16, bool SOFTCAP, int HDIM>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
                          const PrefillParams p) {
+  static_assert(HDIM == 64 || HDIM == 128, "head dim");
+  constexpr int kHalves = HDIM / 64;             // 64-element regions per row
+  constexpr int kLoadBytes = kHalves * kRegion;  // bytes of one Q/K/V tile actually loaded
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -422,11 +427,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The previous item's last QK^T must be done before its Q tiles are replaced.
       if (qloads > 0 && !(ok = warp_wait(bar(B_QE), (qloads - 1) & 1))) break;
       if (lane == 0) {
-        mbar_expect_tx(bar(B_Q), 2 * kTileBytes);
-        tma_load_3d(base + OFF_QA, &tq, bar(B_Q), 0, it.h, it.q_begin + it.row_a);
-        tma_load_3d(base + OFF_QA + kRegion, &tq, bar(B_Q), 64, it.h, it.q_begin + it.row_a);
-        tma_load_3d(base + OFF_QB, &tq, bar(B_Q), 0, it.h, it.q_begin + it.row_b);
-        tma_load_3d(base + OFF_QB + kRegion, &tq, bar(B_Q), 64, it.h, it.q_begin + it.row_b);
+        mbar_expect_tx(bar(B_Q), 2 * kLoadBytes);
+#pragma unroll
+        for (int hf = 0; hf < kHalves; ++hf) {
+          tma_load_3d(base + OFF_QA + hf * kRegion, &tq, bar(B_Q), hf * 64, it.h, it.q_begin + it.row_a);
+          tma_load_3d(base + OFF_QB + hf * kRegion, &tq, bar(B_Q), hf * 64, it.h, it.q_begin + it.row_b);
+        }
       }
       ++qloads;
       for (int i = 0; i < 2 * it.n_all; ++i) {  // K(j), V(j), K(j+1), ...
@@ -437,9 +443,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.table == nullptr) {
           if (lane == 0) {
             const int row = it.k_begin + (it.j_first + (i >> 1)) * BN;
-            mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
-            tma_load_3d(dst, map, bar(B_FULL + slot), 0, it.kh, row);
-            tma_load_3d(dst + kRegion, map, bar(B_FULL + slot), 64, it.kh, row);
+            mbar_expect_tx(bar(B_FULL + slot), kLoadBytes);
+#pragma unroll
+            for (int hf = 0; hf < kHalves; ++hf)
+              tma_load_3d(dst + hf * kRegion, map, bar(B_FULL + slot), hf * 64, it.kh, row);
           }
         } else {
           // Paged K/V: the tile's 128 keys arrive as page boxes (box_rows
@@ -448,9 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           // which TMA fills with zeros.
           const int nb = BN / p.box_rows;
           const int key0 = (it.j_first + (i >> 1)) * BN;
-          if (lane == 0) mbar_expect_tx(bar(B_FULL + slot), kTileBytes);
+          if (lane == 0) mbar_expect_tx(bar(B_FULL + slot), kLoadBytes);
           __syncwarp();
-          if (lane < 2 * nb) {
+          if (lane < kHalves * nb) {
             const int half = lane / nb, c = lane - half * nb;
             const int pos = key0 + c * p.box_rows;
             const int pg = pos >> p.page_shift;
@@ -471,14 +478,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA
     const uint32_t idesc_qk = f16_idesc(BM, BN, BF16 ? 1 : 0, 0);
-    const uint32_t idesc_pv = f16_idesc(BM, HD, BF16 ? 1 : 0, 1);
+    const uint32_t idesc_pv = f16_idesc(BM, HDIM, BF16 ? 1 : 0, 1);
     const uint32_t tSA = tmem, tSB = tmem + 128, tOA = tmem + 256, tOB = tmem + 384;
     auto slot_addr = [&](uint32_t item) { return base + OFF_RING + (item % NSLOT) * kTileBytes; };
     auto wait_item = [&](uint32_t item) { return warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1); };
     auto qk = [&](uint32_t q_off, uint32_t kaddr, uint32_t d, int sfbar) {
       if (lane == 0) {
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
+        for (int kk = 0; kk < HDIM / 16; ++kk) {
           const uint64_t a = sw128_desc(base + q_off + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
@@ -671,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // and PV(j-1) completed before S(j) was signalled.
         if (jj > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < HDIM / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
@@ -696,8 +703,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint8_t* vrow = gbase + OFF_RING + (item % NSLOT) * kTileBytes + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(vrow + kRegion + c * 16) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+              for (int hf = 0; hf < kHalves; ++hf)
+                *reinterpret_cast<uint4*>(vrow + hf * kRegion + c * 16) = make_uint4(0, 0, 0, 0);
             }
           }
           fence_proxy_async_smem();  // generic stores -> the MMA's async-proxy reads
@@ -730,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
       }
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < HDIM / 32; ++c) {
         uint32_t r[32];
         if (n_x > 0) {
           tmem_ld32(tO + c * 32, r);
@@ -759,8 +767,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           const uint32_t sa = smem_addr(stg);
-          tma_store_3d(&to, sa, 0, h, it.q_begin + wrow0);
-          tma_store_3d(&to, sa + 4096, 64, h, it.q_begin + wrow0);
+#pragma unroll
+          for (int hf = 0; hf < kHalves; ++hf) tma_store_3d(&to, sa + hf * 4096, hf * 64, h, it.q_begin + wrow0);
           bulk_commit();
         }
       }
@@ -779,17 +787,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------- host helpers
 // Paged [pages, page, heads, 128] cache -> 4-D map (dims, heads, token in page,
 // page), box {64, 1, box_rows, 1}.
-int make_page_map(CUtensorMap* map, const void* ptr, int dtype, int64_t heads, int64_t page, int64_t pages,
-                  int64_t s_page, int64_t s_tok, int64_t s_head, int box_rows) {
-  const uint64_t dims[4] = {(uint64_t)HD, (uint64_t)heads, (uint64_t)page, (uint64_t)pages};
+int make_page_map(CUtensorMap* map, const void* ptr, int dtype, int64_t dim, int64_t heads, int64_t page,
+                  int64_t pages, int64_t s_page, int64_t s_tok, int64_t s_head, int box_rows) {
+  const uint64_t dims[4] = {(uint64_t)dim, (uint64_t)heads, (uint64_t)page, (uint64_t)pages};
   const uint64_t strides[3] = {(uint64_t)(s_head * 2), (uint64_t)(s_tok * 2), (uint64_t)(s_page * 2)};
   const uint32_t box[4] = {64, 1, (uint32_t)box_rows, 1};
   return encode_tensor_map(map, dtype, 4, ptr, dims, strides, box, true);
 }
 // [rows, heads, 128] tensor with unit inner stride -> 3-D map, box {64, 1, 128}.
-int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t rows, int64_t heads, int64_t s_row,
-             int64_t s_head, int box_rows = BM) {
-  const uint64_t dims[3] = {(uint64_t)HD, (uint64_t)heads, (uint64_t)rows};
+int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t dim, int64_t rows, int64_t heads,
+             int64_t s_row, int64_t s_head, int box_rows = BM) {
+  const uint64_t dims[3] = {(uint64_t)dim, (uint64_t)heads, (uint64_t)rows};
   const uint64_t strides[2] = {(uint64_t)(s_head * 2), (uint64_t)(s_row * 2)};
   const uint32_t box[3] = {64, 1, (uint32_t)box_rows};
   return encode_tensor_map(map, dtype, 3, ptr, dims, strides, box, true);
@@ -801,7 +809,7 @@ bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
 int prefill_sm100_supported(const AttnParams& p) {
   if (!(p.qt == FA_BF16 || p.qt == FA_F16) || p.kt != p.qt || p.vt != p.qt || p.ot != p.qt) return 0;
-  if (p.DQ != HD || p.DV != HD) return 0;
+  if (p.DQ != p.DV || (p.DQ != 64 && p.DQ != 128)) return 0;
   if (p.paged) {
     // Paged K/V: power-of-two pages of >= 8 tokens (whole 1024-byte swizzle
     // atoms per box), a page stride TMA can address.
@@ -838,25 +846,25 @@ int prefill_timeout_flag(bool clear) {
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   CUtensorMap mq, mk, mv;
   if (p.T <= 0) return fail(FA_ERR_INVALID, "prefill needs query rows");
-  int rc = make_map(&mq, p.q, p.qt, p.T, p.HQ, p.qs0, p.qs1);
+  int rc = make_map(&mq, p.q, p.qt, p.DQ, p.T, p.HQ, p.qs0, p.qs1);
   if (rc) return rc;
   int page_shift = 0, box_rows = 0;
   if (p.paged) {
     while ((1 << page_shift) < p.page) ++page_shift;
     box_rows = p.page < BN ? p.page : BN;
-    rc = make_page_map(&mk, p.k, p.kt, p.HK, p.page, p.k_pages, p.ks0, p.ks1, p.ks2, box_rows);
+    rc = make_page_map(&mk, p.k, p.kt, p.DQ, p.HK, p.page, p.k_pages, p.ks0, p.ks1, p.ks2, box_rows);
     if (rc) return rc;
-    rc = make_page_map(&mv, p.v, p.vt, p.HK, p.page, p.k_pages, p.vs0, p.vs1, p.vs2, box_rows);
+    rc = make_page_map(&mv, p.v, p.vt, p.DV, p.HK, p.page, p.k_pages, p.vs0, p.vs1, p.vs2, box_rows);
     if (rc) return rc;
   } else {
     if (p.k_rows <= 0) return fail(FA_ERR_INVALID, "prefill needs packed K/V rows");
-    rc = make_map(&mk, p.k, p.kt, p.k_rows, p.HK, p.ks1, p.ks2);
+    rc = make_map(&mk, p.k, p.kt, p.DQ, p.k_rows, p.HK, p.ks1, p.ks2);
     if (rc) return rc;
-    rc = make_map(&mv, p.v, p.vt, p.k_rows, p.HK, p.vs1, p.vs2);
+    rc = make_map(&mv, p.v, p.vt, p.DV, p.k_rows, p.HK, p.vs1, p.vs2);
     if (rc) return rc;
   }
   CUtensorMap mo;  // output tile stores: 32 rows x 64 head dims per box
-  rc = make_map(&mo, p.out, p.ot, p.T, p.HQ, p.os0, p.os1, 32);
+  rc = make_map(&mo, p.out, p.ot, p.DV, p.T, p.HQ, p.os0, p.os1, 32);
   if (rc) return rc;
   PrefillParams pp{};
   pp.out = p.out; pp.os0 = p.os0; pp.os1 = p.os1;
@@ -881,8 +889,12 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.scale = p.scale;
   pp.softcap = p.softcap;
   const bool cap = p.softcap > 0.f;
-  auto kernel = p.qt == FA_BF16 ? (cap ? prefill_sm100_kernel<true, true> : prefill_sm100_kernel<true, false>)
-                                : (cap ? prefill_sm100_kernel<false, true> : prefill_sm100_kernel<false, false>);
+  auto pick = [&](auto hd) {
+    constexpr int H = decltype(hd)::value;
+    return p.qt == FA_BF16 ? (cap ? prefill_sm100_kernel<true, true, H> : prefill_sm100_kernel<true, false, H>)
+                           : (cap ? prefill_sm100_kernel<false, true, H> : prefill_sm100_kernel<false, false, H>);
+  };
+  auto kernel = p.DQ == 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 128>{});
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
   // The warpgroups' setmaxnreg split assumes exactly kLaunchRegs registers per

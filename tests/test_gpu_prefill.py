@@ -214,3 +214,40 @@ def test_paged_prefill_features(device, dtype):
                           softcap=20.0, sinks=sinks, k_descale=kd, v_descale=vd)
     assert_attention_close(out, ref, dtype)
     assert_lse_close(lse, refl)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("causal", [True, False])
+def test_head_dim_64_on_tensor_core_path(device, dtype, causal):
+    qlens, klens = [1, 127, 128, 129, 700, 5], [1, 127, 300, 129, 1000, 64]
+    g = torch.Generator().manual_seed(41)
+    q = torch.randn(sum(qlens), 8, 64, generator=g).to(dtype).to(device)
+    k = torch.randn(sum(klens), 2, 64, generator=g).to(dtype).to(device)
+    v = torch.randn(sum(klens), 2, 64, generator=g).to(dtype).to(device)
+    cq, ck = cu(qlens, device), cu(klens, device)
+    out, lse = flash_attn_varlen_func(q, k, v, cq, ck, max(qlens), max(klens), causal=causal,
+                                      return_softmax_lse=True)
+    ref, refl = reference(q, k, v, cq, ck, causal=causal)
+    assert_attention_close(out, ref, dtype)
+    assert_lse_close(lse, refl)
+
+
+def test_head_dim_64_paged_softcap_window_sinks(device):
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_attention
+    qlens, klens = [64, 400], [300, 1100]
+    g = torch.Generator().manual_seed(42)
+    columns = 1100 // 16 + 2
+    table = torch.randperm(2 * columns, generator=g)[:2 * columns].int().reshape(2, columns).to(device)
+    k = torch.randn(2 * columns, 16, 4, 64, generator=g).to(torch.bfloat16).to(device)
+    v = torch.randn_like(k)
+    q = (torch.randn(sum(qlens), 16, 64, generator=g) * 2).to(torch.bfloat16).to(device)
+    cq = cu(qlens, device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    sinks = torch.linspace(-1, 1, 16, device=device)
+    out, lse = vllm_attention(q, k, v, max(qlens), cq, max(klens), seqused_k=used, block_table=table,
+                              causal=True, window_size=[200, 0], softcap=10.0, s_aux=sinks,
+                              return_softmax_lse=True)
+    ref, refl = reference(q, k, v, cq, used_k=used, block_table=table, causal=True, window=(200, 0),
+                          softcap=10.0, sinks=sinks)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
