@@ -216,7 +216,20 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
 
 int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
   *plan = Plan{kRouteGeneric, 1, 0, 0, 0};
-  const bool decode = a->max_seqlen_q == 1 && !a->deterministic && !present(a->alibi_slopes) && a->mask_kind == 0;
+  // Batch-invariant mode (deterministic, or num_splits == 1 as vLLM's
+  // batch-invariant path passes it): the kernel choice depends on dtypes and
+  // features only, never on the batch's max_seqlen_q, and every row reduces
+  // its keys in one fixed order. The tensor-core prefill qualifies (a row's
+  // key tiles depend only on its own request); otherwise the generic kernel
+  // with one split.
+  if (a->deterministic || a->num_splits == 1) {
+    if (prefill_sm100_supported(p)) {
+      plan->route = kRoutePrefill;
+      plan->part_bytes = 256;  // persistent-scheduler work counter
+    }
+    return FA_OK;
+  }
+  const bool decode = a->max_seqlen_q == 1 && !present(a->alibi_slopes) && a->mask_kind == 0;
   if (decode) {
     const int eff = a->window_left >= 0 ? std::min(a->max_seqlen_k, a->window_left + 1) : a->max_seqlen_k;
     if (decode_mma_supported(p)) {
@@ -232,15 +245,14 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
       plan->splits = a->num_splits > 0 ? a->num_splits : std::max(1, std::min(32, (eff + 255) / 256));
     }
   } else {
-    if (!a->deterministic && a->num_splits <= 1 && prefill_sm100_supported(p)) {
+    if (a->num_splits == 0 && prefill_sm100_supported(p)) {
       plan->route = kRoutePrefill;
       plan->splits = 1;
       plan->part_bytes = 256;  // persistent-scheduler work counter
       return FA_OK;
     } else {
-      const bool vector = a->deterministic || a->max_seqlen_q == 1 || std::max(p.DQ, p.DV) > 256;
-      plan->splits = a->deterministic ? 1
-                     : a->num_splits > 0 ? a->num_splits
+      const bool vector = a->max_seqlen_q == 1 || std::max(p.DQ, p.DV) > 256;
+      plan->splits = a->num_splits > 0 ? a->num_splits
                      : vector ? std::min(32, std::max(1, (a->max_seqlen_k + 255) / 256)) : 1;
     }
   }

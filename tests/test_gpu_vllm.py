@@ -161,3 +161,46 @@ def test_num_splits_one_is_batch_invariant(device):
                                     max_seqlen_k=513, cu_seqlens_k=torch.tensor([0, 513], device=device, dtype=torch.int32),
                                     causal=True, num_splits=1)
     torch.testing.assert_close(single, batched[:1], atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("mode", ["deterministic", "num_splits_1"])
+@pytest.mark.parametrize("paged", [False, True])
+def test_batch_invariance_on_tensor_core_path(device, mode, paged):
+    # Each request's rows are bitwise identical whether it runs alone or in a
+    # batch with decode (q_len 1) and prefill requests of other lengths.
+    g = torch.Generator().manual_seed(51)
+    qlens, klens = [1, 37, 1, 300], [900, 400, 33, 300]
+    H, HK, D, page = 8, 2, 128, 16
+    q = torch.randn(sum(qlens), H, D, generator=g).to(torch.bfloat16).to(device)
+    flags = dict(deterministic=True) if mode == "deterministic" else dict(num_splits=1)
+    if paged:
+        cols = max(klens) // page + 1
+        kc = torch.randn(len(klens) * cols, page, HK, D, generator=g).to(torch.bfloat16).to(device)
+        vc = torch.randn_like(kc)
+        table = torch.randperm(len(klens) * cols, generator=g).int().reshape(len(klens), cols).to(device)
+    else:
+        k = torch.randn(sum(klens), HK, D, generator=g).to(torch.bfloat16).to(device)
+        v = torch.randn_like(k)
+    cq = torch.tensor([0, *torch.tensor(qlens).cumsum(0).tolist()], dtype=torch.int32, device=device)
+    ck = torch.tensor([0, *torch.tensor(klens).cumsum(0).tolist()], dtype=torch.int32, device=device)
+
+    def run(rows):
+        sub_q = torch.cat([q[cq[b]:cq[b + 1]] for b in rows])
+        sq = torch.tensor([0, *torch.tensor([qlens[b] for b in rows]).cumsum(0).tolist()], dtype=torch.int32,
+                          device=device)
+        if paged:
+            used = torch.tensor([klens[b] for b in rows], dtype=torch.int32, device=device)
+            return flash_attn_varlen_func(sub_q, kc, vc, max(qlens[b] for b in rows), sq,
+                                          max(klens[b] for b in rows), seqused_k=used,
+                                          block_table=table[rows], causal=True, **flags)
+        sub_k = torch.cat([k[ck[b]:ck[b + 1]] for b in rows])
+        sub_v = torch.cat([v[ck[b]:ck[b + 1]] for b in rows])
+        sk = torch.tensor([0, *torch.tensor([klens[b] for b in rows]).cumsum(0).tolist()], dtype=torch.int32,
+                          device=device)
+        return flash_attn_varlen_func(sub_q, sub_k, sub_v, max(qlens[b] for b in rows), sq,
+                                      max(klens[b] for b in rows), cu_seqlens_k=sk, causal=True, **flags)
+
+    batched = run(list(range(len(qlens))))
+    for b in range(len(qlens)):
+        alone = run([b])
+        assert torch.equal(alone, batched[cq[b]:cq[b + 1]]), b
