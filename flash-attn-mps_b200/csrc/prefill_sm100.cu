@@ -286,11 +286,22 @@ __device__ __forceinline__ void item_store(volatile int* d, const Item& it) {
   d[11] = it.a0; d[12] = it.a1; d[13] = it.b0; d[14] = it.b1; d[15] = it.j_first; d[16] = it.n_all;
   d[17] = __float_as_int(it.qk_scale); d[18] = __float_as_int(it.vscale); d[19] = __float_as_int(it.sink_l2);
 }
+// Five 16-byte shared loads (issued together) after the slot's full barrier.
 __device__ __forceinline__ void item_load(const volatile int* d, Item& it) {
-  it.valid = d[0]; it.b = d[1]; it.h = d[2]; it.kh = d[3]; it.q_begin = d[4]; it.q_len = d[5];
-  it.k_begin = d[6]; it.k_len = d[7]; it.row_a = d[8]; it.row_b = d[9]; it.causal = d[10];
-  it.a0 = d[11]; it.a1 = d[12]; it.b0 = d[13]; it.b1 = d[14]; it.j_first = d[15]; it.n_all = d[16];
-  it.qk_scale = __int_as_float(d[17]); it.vscale = __int_as_float(d[18]); it.sink_l2 = __int_as_float(d[19]);
+  int4 w[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    asm volatile("ld.shared.v4.s32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(w[i].x), "=r"(w[i].y), "=r"(w[i].z), "=r"(w[i].w)
+                 : "r"(smem_addr(const_cast<const int*>(d) + 4 * i))
+                 : "memory");
+  }
+  it.valid = w[0].x; it.b = w[0].y; it.h = w[0].z; it.kh = w[0].w;
+  it.q_begin = w[1].x; it.q_len = w[1].y; it.k_begin = w[1].z; it.k_len = w[1].w;
+  it.row_a = w[2].x; it.row_b = w[2].y; it.causal = w[2].z; it.a0 = w[2].w;
+  it.a1 = w[3].x; it.b0 = w[3].y; it.b1 = w[3].z; it.j_first = w[3].w;
+  it.n_all = w[4].x; it.qk_scale = __int_as_float(w[4].y); it.vscale = __int_as_float(w[4].z);
+  it.sink_l2 = __int_as_float(w[4].w);
 }
 
 __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
@@ -348,7 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t holder = base + OFF_BAR + 8u * B_COUNT;
   volatile uint32_t* holder_ptr = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT);
   volatile int* wring = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * B_COUNT + 16);
-  volatile int* iring = reinterpret_cast<volatile int*>(gbase + OFF_BAR + 8 * B_COUNT + 32);  // [NWORK][20]
+  volatile int* iring =  // [NWORK][20], 16-byte aligned
+      reinterpret_cast<volatile int*>(gbase + ((OFF_BAR + 8 * B_COUNT + 32 + 15) & ~15));
   // Work ids flow from the TMA warp (which claims them with an atomic counter,
   // heaviest first) to the MMA warp and the 8 softmax warps through a ring.
   auto next_work = [&](uint32_t& cnt, Item& it) -> int {
@@ -737,20 +749,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) bulk_wait_read();  // this warp's previous stores have read the buffer
         __syncwarp();
       }
+      // The whole O row in registers with one TMEM round trip (also when this
+      // tile saw no key: the values are then unused, see `have`).
+      uint32_t r[HDIM];
+      {
+        tmem_ld32_at<0>(tO, r);
+        tmem_ld32_at<32>(tO + 32, r);
+        if constexpr (HDIM == 128) {
+          tmem_ld32_at<64>(tO + 64, r);
+          tmem_ld32_at<96>(tO + 96, r);
+        }
+        tmem_wait_ld();
+      }
 #pragma unroll
       for (int c = 0; c < HDIM / 32; ++c) {
-        uint32_t r[32];
-        if (n_x > 0) {
-          tmem_ld32(tO + c * 32, r);
-          tmem_wait_ld();
-        }
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           uint32_t wv[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const float a = have ? __uint_as_float(r[v * 8 + 2 * i]) * inv : 0.f;
-            const float bb = have ? __uint_as_float(r[v * 8 + 2 * i + 1]) * inv : 0.f;
+            const float a = have ? __uint_as_float(r[c * 32 + v * 8 + 2 * i]) * inv : 0.f;
+            const float bb = have ? __uint_as_float(r[c * 32 + v * 8 + 2 * i + 1]) * inv : 0.f;
             wv[i] = pack_p<BF16>(a, bb);
           }
           const uint4 val = make_uint4(wv[0], wv[1], wv[2], wv[3]);
