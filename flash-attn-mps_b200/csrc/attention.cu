@@ -89,7 +89,7 @@ int encode_tensor_map(void* map, int dtype, int rank, const void* ptr, const uin
 
 namespace {
 
-enum Route { kRouteGeneric = 0, kRouteDecode = 1, kRoutePrefill = 2 };
+enum Route { kRouteGeneric = 0, kRouteDecode = 1, kRoutePrefill = 2, kRouteMma = 3 };
 
 struct Plan {
   int route;
@@ -220,17 +220,18 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
   // batch-invariant path passes it): the kernel choice depends on dtypes and
   // features only, never on the batch's max_seqlen_q, and every row reduces
   // its keys in one fixed order. The tensor-core prefill qualifies (a row's
-  // key tiles depend only on its own request); otherwise the generic kernel
-  // with one split.
-  if (a->deterministic || a->num_splits == 1) {
-    if (prefill_sm100_supported(p)) {
-      plan->route = kRoutePrefill;
-      plan->part_bytes = 256;  // persistent-scheduler work counter
-    }
+  // key tiles depend only on its own request); otherwise the mma.sync or the
+  // generic kernel with one split.
+  const bool invariant = a->deterministic || a->num_splits == 1;
+  if (invariant && prefill_sm100_supported(p)) {
+    plan->route = kRoutePrefill;
+    plan->part_bytes = 256;  // persistent-scheduler work counter
     return FA_OK;
   }
   const bool decode = a->max_seqlen_q == 1 && !present(a->alibi_slopes) && a->mask_kind == 0;
-  if (decode) {
+  if (invariant) {
+    plan->splits = 1;  // generic or mma.sync kernel, one split
+  } else if (decode) {
     const int eff = a->window_left >= 0 ? std::min(a->max_seqlen_k, a->window_left + 1) : a->max_seqlen_k;
     if (decode_mma_supported(p)) {
       plan->route = kRouteDecode;
@@ -255,6 +256,13 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
       plan->splits = a->num_splits > 0 ? a->num_splits
                      : vector ? std::min(32, std::max(1, (a->max_seqlen_k + 255) / 256)) : 1;
     }
+  }
+  // f16/bf16 cases left to the generic kernel run on the mma.sync tensor-core
+  // kernel when its head dims and strides fit (same splits, same semantics).
+  if (plan->route == kRouteGeneric) {
+    AttnParams q = p;
+    q.splits = plan->splits;
+    if (mma_attention_supported(q)) plan->route = kRouteMma;
   }
   if (plan->splits > 1) {
     plan->part_bytes = ((size_t)plan->splits * p.T * p.HQ * p.DV * sizeof(float) + 255) / 256 * 256;
@@ -323,6 +331,7 @@ extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
   switch (plan.route) {
     case kRouteDecode: rc = launch_decode_mma(p, plan.splits, plan.span, st); break;
     case kRoutePrefill: rc = launch_prefill_sm100(p, st); break;
+    case kRouteMma: rc = launch_mma_attention(p, st); break;
     default: rc = launch_generic_attention(p, st); break;
   }
   if (rc) return rc;

@@ -69,6 +69,8 @@ int decode_default_splits(const AttnParams& p, int* span);
 // tcgen05/TMEM/TMA prefill kernel.
 int prefill_sm100_supported(const AttnParams& p);
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream);
+int mma_attention_supported(const AttnParams& p);
+int launch_mma_attention(const AttnParams& p, cudaStream_t stream);
 // Timed-out pipeline waits recorded by the prefill / TMA decode kernels on the
 // current device (1 = some wait gave up, 0 = none, -1 = CUDA error).
 int prefill_timeout_flag(bool clear);
