@@ -79,7 +79,10 @@ struct Layout {
 
 // PREC (fp32 outputs): P = hi + lo in two 16-bit halves, two PV MMAs, so the
 // probabilities keep ~16 (bf16) / ~22 (f16) bits as an fp32 reference expects.
-template <typename T, bool KV8, int DQ, int DV, bool PREC>
+// SIMPLE: no ALiBi, softcap or mask descriptor (causal, windows, lengths
+// only): scores are scaled in one multiply and masked only in warp tiles that
+// straddle a causal / window / length edge.
+template <typename T, bool KV8, int DQ, int DV, bool PREC, bool SIMPLE>
 __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParams p) {
   using L = Layout<KV8, DQ, DV>;
   constexpr bool kQRegs = DQ <= 128;  // Q fragments kept in registers
@@ -224,21 +227,51 @@ __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParam
 
     // Scores with the reference's features, then the online softmax (log2).
     float mx[2] = {-INFINITY, -INFINITY};
+    if constexpr (SIMPLE) {
+      // Visible keys of the warp's first and last row; the tile needs no
+      // per-element test when every (row, key) pair is visible.
+      const int q_lo = q_block + warp * 16, q_hi = min(q_lo + 15, q_len - 1);
+      const int off = k_len - q_len, key0 = kb * kBN, key1 = key0 + kBN - 1;
+      bool full = q_hi >= q_lo && key1 < k_len;
+      if (causal) full = full && key1 <= q_lo + off;
+      if (p.win_r >= 0) full = full && key1 <= q_lo + off + p.win_r;
+      if (p.win_l >= 0) full = full && key0 >= q_hi + off - p.win_l;
+      const float sl2 = scale * kLog2e;
 #pragma unroll
-    for (int n = 0; n < kBN / 8; ++n) {
+      for (int n = 0; n < kBN / 8; ++n) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int row = e >> 1;
-        const int q = q_block + warp * 16 + g + 8 * row;
-        const int t = kb * kBN + n * 8 + 2 * qd + (e & 1);
-        const int q_abs = q + k_len - q_len;
-        float x = s[n][e] * scale;
-        if (p.softcap > 0.f) x = p.softcap * tanhf(x / p.softcap);
-        x -= slope * fabsf((float)(q_abs - t));
-        const bool keep = q < q_len && t < k_len && allowed_key(p, b, t, q_abs, (int64_t)q_begin + q, causal);
-        x = keep ? x * kLog2e : -INFINITY;
-        s[n][e] = x;
-        mx[row] = fmaxf(mx[row], x);
+        for (int e = 0; e < 4; ++e) {
+          const int row = e >> 1;
+          float x = s[n][e] * sl2;
+          if (!full) {
+            const int q = q_block + warp * 16 + g + 8 * row;
+            const int t = key0 + n * 8 + 2 * qd + (e & 1);
+            const int diff = q + off - t;
+            const bool keep = q < q_len && t < k_len && (!causal || diff >= 0) &&
+                              (p.win_l < 0 || diff <= p.win_l) && (p.win_r < 0 || -diff <= p.win_r);
+            x = keep ? x : -INFINITY;
+          }
+          s[n][e] = x;
+          mx[row] = fmaxf(mx[row], x);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int n = 0; n < kBN / 8; ++n) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = e >> 1;
+          const int q = q_block + warp * 16 + g + 8 * row;
+          const int t = kb * kBN + n * 8 + 2 * qd + (e & 1);
+          const int q_abs = q + k_len - q_len;
+          float x = s[n][e] * scale;
+          if (p.softcap > 0.f) x = p.softcap * tanhf(x / p.softcap);
+          x -= slope * fabsf((float)(q_abs - t));
+          const bool keep = q < q_len && t < k_len && allowed_key(p, b, t, q_abs, (int64_t)q_begin + q, causal);
+          x = keep ? x * kLog2e : -INFINITY;
+          s[n][e] = x;
+          mx[row] = fmaxf(mx[row], x);
+        }
       }
     }
     float factor[2], nsafe[2];
@@ -337,7 +370,10 @@ __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParam
 template <typename T, bool KV8, int DQ, int DV>
 int launch_shape(const AttnParams& p, cudaStream_t stream) {
   constexpr int smem = Layout<KV8, DQ, DV>::kSmem;
-  auto kernel = p.ot == FA_F32 ? mma_attention_kernel<T, KV8, DQ, DV, true> : mma_attention_kernel<T, KV8, DQ, DV, false>;
+  const bool simple = p.alibi == nullptr && p.softcap <= 0.f && p.mask == 0;
+  auto kernel = p.ot == FA_F32 ? mma_attention_kernel<T, KV8, DQ, DV, true, false>
+                : simple       ? mma_attention_kernel<T, KV8, DQ, DV, false, true>
+                               : mma_attention_kernel<T, KV8, DQ, DV, false, false>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "mma attention smem attribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)((p.max_q + kBM - 1) / kBM), (unsigned)p.HQ, (unsigned)((int64_t)p.B * p.splits));
