@@ -356,6 +356,90 @@ __global__ void __launch_bounds__(256) rotary_kernel(RotaryArgs a) {
   }
 }
 
+// ------------------------------------------------- fused rotary + append
+// Rotates the new K at lengths[b] + j, rounds it to K's dtype (what the
+// separate rotary writes), appends it (E4M3-quantised for an FP8 cache),
+// appends V, and rotates Q into q_out at lengths[b] (+ j when advance_q): the
+// same values as rotary followed by append, in one pass (blockIdx.y = 0 K,
+// 1 V, 2 Q). cos/sin may be any float dtype (read as float32).
+struct RopeArgs {
+  const void* cos; const void* sin; int32_t cdtype;
+  int64_t cs0, cs1, ss0, ss1;
+  int32_t half, interleaved, advance_q;
+  int64_t batch;
+  const void* q; void* q_out; int32_t qdtype, QS, QH, QD;
+  int64_t qs0, qs1, qs2, qs3, qo0, qo1, qo2, qo3;
+  int64_t q_units;
+};
+
+__device__ __forceinline__ float round_to(int dtype, float v) {
+  if (dtype == FA_F16) return __half2float(__float2half_rn(v));
+  if (dtype == FA_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  return v;
+}
+
+// Rotated value of element d of row `src` (element strides ds) at position pos.
+__device__ __forceinline__ float rope_value(const RopeArgs& r, const void* x, int dtype, int64_t src, int64_t ds,
+                                            int d, int64_t pos) {
+  const int pair = r.interleaved ? d / 2 : d % r.half;
+  const bool second = r.interleaved ? (d & 1) : d >= r.half;
+  const int other = r.interleaved ? (second ? d - 1 : d + 1) : (second ? d - r.half : d + r.half);
+  const float c = load_float(r.cos, r.cdtype, pos * r.cs0 + pair * r.cs1);
+  const float sn = load_float(r.sin, r.cdtype, pos * r.ss0 + pair * r.ss1);
+  const float xv = load_float(x, dtype, src + d * ds);
+  const float yv = load_float(x, dtype, src + other * ds);
+  const float ys = __fmul_rn(yv, sn);
+  return __fadd_rn(__fmul_rn(xv, c), second ? ys : -ys);
+}
+
+__global__ void __launch_bounds__(256) rotary_append_kernel(AppendArgs a, RopeArgs r) {
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  if (blockIdx.y == 2) {
+    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < r.q_units; u += step) {
+      const int d = (int)(u % r.QD);
+      int64_t t = u / r.QD;
+      const int h = (int)(t % r.QH); t /= r.QH;
+      const int j = (int)(t % r.QS);
+      const int64_t b = t / r.QS;
+      const int64_t src = b * r.qs0 + j * r.qs1 + h * r.qs2;
+      const int64_t dst = b * r.qo0 + j * r.qo1 + h * r.qo2 + d * r.qo3;
+      const int64_t pos = (int64_t)a.lengths[b * a.len_stride] + (r.advance_q ? j : 0);
+      const float value = d < 2 * r.half ? rope_value(r, r.q, r.qdtype, src, r.qs3, d, pos)
+                                         : load_float(r.q, r.qdtype, src + d * r.qs3);
+      store_float(r.q_out, r.qdtype, dst, value);
+    }
+    return;
+  }
+  const AppendSide& s = a.side[blockIdx.y];
+  if (s.x == nullptr) return;
+  const bool rotate = blockIdx.y == 0;
+  const int64_t total = r.batch * s.S * (int64_t)s.H * s.D;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < total; u += step) {
+    const int d = (int)(u % s.D);
+    int64_t t = u / s.D;
+    const int h = (int)(t % s.H); t /= s.H;
+    const int j = (int)(t % s.S);
+    const int64_t b = t / s.S;
+    const int64_t row = a.remap ? (int64_t)a.batch_idx[b * a.bi_stride] : b;
+    const int64_t pos = (int64_t)a.lengths[b * a.len_stride] + j;
+    const int64_t capacity = a.paged ? (int64_t)a.pages_per_seq * a.P : a.P;
+    if (row < 0 || row >= a.rows || pos < 0 || pos >= capacity) continue;
+    const int64_t block = a.paged ? (int64_t)a.table[row * a.bt0 + (pos / a.P) * a.bt1] : row;
+    const int64_t offset = a.paged ? pos % a.P : pos;
+    if (block < 0 || block >= a.blocks) continue;
+    const int64_t src = b * s.xs0 + j * s.xs1 + h * s.xs2;
+    const int64_t dst = block * s.cs0 + offset * s.cs1 + h * s.cs2 + d * s.cs3;
+    const float value = rotate && d < 2 * r.half ? round_to(s.xdtype, rope_value(r, s.x, s.xdtype, src, s.xs3, d, pos))
+                                                 : load_float(s.x, s.xdtype, src + d * s.xs3);
+    if (s.fp8) {
+      const float scale = s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+      reinterpret_cast<uint8_t*>(s.cache)[dst] = float_to_e4m3_sat(__fdiv_rn(value, scale));
+    } else {
+      store_float(s.cache, s.xdtype, dst, value);
+    }
+  }
+}
+
 int grid_for(int64_t units) {
   int64_t blocks = (units + 255) / 256;
   const int64_t cap = (int64_t)sm_count() * 8;
@@ -490,6 +574,81 @@ extern "C" int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
     append_kernel<<<dim3(grid_for(per[i].units), 1), 256, 0, st>>>(per[i]);
     FAB_LAUNCH_CHECK("append_kvcache launch");
   }
+  return FA_OK;
+}
+
+extern "C" int fa_rotary_append_kvcache(const fa_tensor* q, const fa_tensor* q_out,
+                                        const fa_tensor* key, const fa_tensor* value,
+                                        const fa_tensor* k_cache, const fa_tensor* v_cache,
+                                        const fa_tensor* lengths, const fa_tensor* cache_batch_idx,
+                                        const fa_tensor* block_table,
+                                        const fa_tensor* k_scale, const fa_tensor* v_scale,
+                                        const fa_tensor* cos, const fa_tensor* sin,
+                                        int32_t interleaved, int32_t advance_q, void* stream) {
+  FAB_CHECK_ARG(present(lengths) && lengths->dtype == FA_I32 && lengths->ndim == 1,
+                "lengths must be int32 [B]");
+  const int64_t batch = lengths->shape[0];
+  FAB_CHECK_ARG(present(key) && present(value), "rotary append needs new k and v");
+  AppendArgs a{};
+  int rc = prepare_append_side(key, k_cache, k_scale, batch, &a.side[0]);
+  if (rc) return rc;
+  rc = prepare_append_side(value, v_cache, v_scale, batch, &a.side[1]);
+  if (rc) return rc;
+  FAB_CHECK_ARG(present(cos) && present(sin) && cos->ndim == 2 && sin->ndim == 2 && is_float(cos->dtype) &&
+                    sin->dtype == cos->dtype && cos->shape[0] == sin->shape[0] && cos->shape[1] == sin->shape[1],
+                "rotary cosine/sine must be float [positions, rotary_dim/2] of one dtype");
+  FAB_CHECK_ARG(cos->shape[1] * 2 <= key->shape[3], "rotary dimension exceeds head dimension");
+  a.lengths = reinterpret_cast<const int32_t*>(lengths->ptr);
+  a.len_stride = lengths->stride[0];
+  a.paged = present(block_table);
+  a.remap = !a.paged && present(cache_batch_idx);
+  if (a.remap) {
+    FAB_CHECK_ARG(cache_batch_idx->dtype == FA_I32 && cache_batch_idx->ndim == 1 &&
+                      cache_batch_idx->shape[0] == batch, "cache_batch_idx must be int32 [B]");
+    a.batch_idx = reinterpret_cast<const int32_t*>(cache_batch_idx->ptr);
+    a.bi_stride = cache_batch_idx->stride[0];
+  }
+  if (a.paged) {
+    FAB_CHECK_ARG(block_table->dtype == FA_I32 && block_table->ndim == 2,
+                  "block_table must have shape [cache_batch, blocks_per_sequence]");
+    a.table = reinterpret_cast<const int32_t*>(block_table->ptr);
+    a.bt0 = block_table->stride[0];
+    a.bt1 = block_table->stride[1];
+    a.pages_per_seq = (int32_t)block_table->shape[1];
+    a.rows = block_table->shape[0];
+  } else {
+    a.rows = k_cache->shape[0];
+  }
+  a.P = (int32_t)k_cache->shape[1];
+  a.blocks = k_cache->shape[0];
+  RopeArgs r{};
+  r.cos = cos->ptr; r.sin = sin->ptr; r.cdtype = cos->dtype;
+  r.cs0 = cos->stride[0]; r.cs1 = cos->stride[1]; r.ss0 = sin->stride[0]; r.ss1 = sin->stride[1];
+  r.half = (int32_t)cos->shape[1];
+  r.interleaved = interleaved; r.advance_q = advance_q;
+  r.batch = batch;
+  int64_t units = 0;
+  for (int i = 0; i < 2; ++i) {
+    const int64_t n = batch * a.side[i].S * (int64_t)a.side[i].H * a.side[i].D;
+    units = n > units ? n : units;
+  }
+  int sides = 2;
+  if (present(q)) {
+    FAB_CHECK_ARG(present(q_out) && q->ndim == 4 && q_out->ndim == 4 && q->shape[0] == batch &&
+                      q->dtype == q_out->dtype && is_float(q->dtype),
+                  "q and q_out must be float [B,S,H,D] of one dtype");
+    for (int i = 0; i < 4; ++i) FAB_CHECK_ARG(q->shape[i] == q_out->shape[i], "q_out must match q");
+    FAB_CHECK_ARG(cos->shape[1] * 2 <= q->shape[3], "rotary dimension exceeds head dimension");
+    r.q = q->ptr; r.q_out = q_out->ptr; r.qdtype = q->dtype;
+    r.QS = (int32_t)q->shape[1]; r.QH = (int32_t)q->shape[2]; r.QD = (int32_t)q->shape[3];
+    for (int i = 0; i < 4; ++i) { (&r.qs0)[i] = q->stride[i]; (&r.qo0)[i] = q_out->stride[i]; }
+    r.q_units = batch * r.QS * (int64_t)r.QH * r.QD;
+    units = r.q_units > units ? r.q_units : units;
+    sides = 3;
+  }
+  if (units == 0) return FA_OK;
+  rotary_append_kernel<<<dim3(grid_for(units), sides), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, r);
+  FAB_LAUNCH_CHECK("rotary append launch");
   return FA_OK;
 }
 

@@ -133,3 +133,54 @@ def rotary(q, k, cos, sin, cache_seqlens, *, rotary_interleaved=True, causal=Fal
                                       int(advance), _capi.stream_of(x.device)))
         outputs.append(output)
     return tuple(outputs)
+
+
+def rotary_append_kvcache(q, k, v, k_cache, v_cache, cos, sin, cache_seqlens, *, rotary_interleaved=True,
+                          causal=False, window_size=(-1, -1), cache_batch_idx=None, cache_leftpad=None,
+                          block_table=None, k_scale=None, v_scale=None):
+    """``rotary`` of Q and the new K followed by ``append_kvcache`` of (rotated K, V), in one launch.
+
+    Same validation and the same values as the two calls in sequence (the
+    rotated K is rounded to its dtype before it is appended); returns the
+    rotated Q. ``flash_attn_with_kvcache`` uses it when it gets rotary tables
+    and new K/V.
+    """
+    _cuda(q, k, v, cos, sin, k_cache, v_cache, block_table)
+    if q.ndim != 4 or k.ndim != 4 or q.shape[0] != k.shape[0]:
+        raise ValueError("Q/K must have shape [batch, tokens, heads, dim]")
+    if cos.ndim != 2 or sin.shape != cos.shape or cos.shape[1] * 2 > q.shape[-1]:
+        raise ValueError("rotary cosine/sine must have shape [positions, rotary_dim/2]")
+    if cos.shape[1] * 2 > k.shape[-1]:
+        raise ValueError("rotary dimension exceeds head dimension")
+    for x in (q, k):
+        if x.dtype not in _FLOATS:
+            raise TypeError("input dtype must be float16, bfloat16 or float32")
+    if cos.dtype not in _FLOATS or sin.dtype != cos.dtype:
+        cos, sin = cos.float(), sin.float()
+    if v.ndim != 4 or k.shape[:3] != v.shape[:3]:
+        raise ValueError("K/V must have matching [batch, new_tokens, heads, dim] shapes")
+    batch = k.shape[0]
+    lengths = _integers(cache_seqlens, batch, k.device)
+    remap = block_table is None and cache_batch_idx is not None
+    indices = _integers(cache_batch_idx, batch, k.device) if remap else None
+    if cache_leftpad is not None:
+        _integers(cache_leftpad, batch, k.device)
+    if block_table is not None:
+        if block_table.ndim != 2:
+            raise ValueError("block_table must have shape [cache_batch, blocks_per_sequence]")
+        block_table = block_table.to(torch.int32)
+    for x, cache in ((k, k_cache), (v, v_cache)):
+        if cache.ndim != 4 or cache.shape[2:] != x.shape[2:]:
+            raise ValueError("cache must have shape [rows, capacity, heads, dim]")
+        _check_cache_dtype(x, cache)
+    ks = _scale(k_scale, k.shape[2], k.device) if k_cache.dtype == torch.float8_e4m3fn else None
+    vs = _scale(v_scale, v.shape[2], v.device) if v_cache.dtype == torch.float8_e4m3fn else None
+    q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    advance_q = bool(causal) or tuple(window_size) != (-1, -1)
+    t = _capi.tensor
+    args = [t(q), t(q_out), t(k), t(v), t(k_cache), t(v_cache), t(lengths), t(indices), t(block_table),
+            t(ks), t(vs), t(cos), t(sin)]
+    lib = _capi.library()
+    _capi.check(lib.fa_rotary_append_kvcache(*map(_capi.ref, args), int(bool(rotary_interleaved)),
+                                             int(advance_q), _capi.stream_of(q.device)))
+    return q_out

@@ -67,6 +67,7 @@ SIGNATURES = {
     "fa_store_kvcache": [_P(Tensor)] * 7 + [ctypes.c_void_p],
     "fa_append_kvcache": [_P(Tensor)] * 9 + [ctypes.c_void_p],
     "fa_rotary": [_P(Tensor)] * 5 + [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p],
+    "fa_rotary_append_kvcache": [_P(Tensor)] * 13 + [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p],
     "fa_merge_attn_states": [_P(Tensor)] * 6 + [ctypes.c_void_p],
     "fa_merge_partials": [_P(Tensor)] * 4 + [ctypes.c_void_p],
 }

@@ -256,18 +256,22 @@ def flash_attn_with_kvcache(
         raise ValueError("cache_seqlens must be an int or CUDA int32 [B]")
     if (rotary_cos is None) != (rotary_sin is None):
         raise ValueError("rotary_cos and rotary_sin must be provided together")
-    if rotary_cos is not None:
-        if k is None:
-            raise ValueError("rotary embedding requires new k and v")
-        from ._cache import rotary
-        q, k = rotary(q, k, rotary_cos, rotary_sin, lengths, rotary_interleaved=rotary_interleaved,
-                      causal=causal, window_size=window_size)
+    if rotary_cos is not None and k is None:
+        raise ValueError("rotary embedding requires new k and v")
     if k is not None:
         if k.ndim != 4 or v.ndim != 4 or k.shape[0] != batch or v.shape[:3] != k.shape[:3]:
             raise ValueError("new k/v must have matching [B,Snew,Hkv,D] dimensions")
-        from ._cache import append_kvcache
-        append_kvcache(k, v, k_cache, v_cache, lengths, cache_batch_idx=cache_batch_idx,
-                       cache_leftpad=cache_leftpad, block_table=block_table)
+        if rotary_cos is not None:
+            # RoPE of Q and new K fused with the append (one launch, same values).
+            from ._cache import rotary_append_kvcache
+            q = rotary_append_kvcache(q, k, v, k_cache, v_cache, rotary_cos, rotary_sin, lengths,
+                                      rotary_interleaved=rotary_interleaved, causal=causal,
+                                      window_size=window_size, cache_batch_idx=cache_batch_idx,
+                                      cache_leftpad=cache_leftpad, block_table=block_table)
+        else:
+            from ._cache import append_kvcache
+            append_kvcache(k, v, k_cache, v_cache, lengths, cache_batch_idx=cache_batch_idx,
+                           cache_leftpad=cache_leftpad, block_table=block_table)
         lengths = lengths + k.shape[1]
     if block_table is None:
         rows = cache_batch_idx

@@ -189,6 +189,27 @@ int fa_rotary(const fa_tensor* x, const fa_tensor* out,
               void* stream);
 
 /*
+ * Fused RoPE + cache append (what flash_attn_with_kvcache does with rotary
+ * tables and new K/V, in one launch): the new key [B,S,Hkv,Dk] rotated at
+ * lengths[b] + j and rounded to its dtype, then appended like
+ * fa_append_kvcache (E4M3-quantised with k_scale for an FP8 cache); value
+ * appended unchanged; q [B,Sq,H,D] (optional) rotated at lengths[b] (+ j when
+ * advance_q) into q_out. cos/sin: [positions, rotary_dim/2] of any float
+ * dtype. Results equal fa_rotary followed by fa_append_kvcache bit for bit.
+ * No single counterpart in the reference: it fuses flash_attn_mps/_cache.py:
+ * 229-254 (rotary, kernels/cache.metal:58-76) with _cache.py:198-226 (append,
+ * kernels/cache.metal:41-56) as called from interface.py:231-307.
+ */
+int fa_rotary_append_kvcache(const fa_tensor* q, const fa_tensor* q_out,
+                             const fa_tensor* key, const fa_tensor* value,
+                             const fa_tensor* k_cache, const fa_tensor* v_cache,
+                             const fa_tensor* lengths, const fa_tensor* cache_batch_idx,
+                             const fa_tensor* block_table,
+                             const fa_tensor* k_scale, const fa_tensor* v_scale,
+                             const fa_tensor* cos, const fa_tensor* sin,
+                             int32_t interleaved, int32_t advance_q, void* stream);
+
+/*
  * Stable pairwise merge of two attention states: out [T,H,D] and out_lse
  * [H,T] (optional) may alias the left state.
  * Replaces flash_attn_mps/_merge.py:20-41 (merge_attn_states), kernel

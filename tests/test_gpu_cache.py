@@ -187,3 +187,38 @@ def test_rotary_modes_strides_and_partial_head(device, interleaved, mode, dtype)
     torch.testing.assert_close(qr.cpu().double(), torch.from_numpy(qe).to(dtype).double(), **tol)
     torch.testing.assert_close(kr.cpu().double(), torch.from_numpy(ke).to(dtype).double(), **tol)
     assert torch.equal(qr.cpu()[..., 4:], q.cpu()[..., 4:])
+
+
+@pytest.mark.parametrize("cache_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+@pytest.mark.parametrize("paged", [False, True])
+@pytest.mark.parametrize("interleaved", [True, False])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("table_dtype", [torch.float32, torch.bfloat16])
+def test_fused_rotary_append_equals_rotary_then_append(device, cache_dtype, paged, interleaved, causal,
+                                                       table_dtype):
+    from flash_attn_b200._cache import append_kvcache, rotary, rotary_append_kvcache
+    g = torch.Generator().manual_seed(61)
+    B, S, H, HK, D, rot, cap, page = 3, 5, 8, 2, 128, 96, 64, 16
+    q = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).to(device)
+    k = torch.randn(B, S, HK, D, generator=g).to(torch.bfloat16).to(device)
+    v = torch.randn(B, S, HK, D, generator=g).to(torch.bfloat16).to(device)
+    angles = torch.rand(cap + S, rot // 2, generator=g) * 6
+    cos, sin = angles.cos().to(table_dtype).to(device), angles.sin().to(table_dtype).to(device)
+    lengths = torch.tensor([0, 17, 40], dtype=torch.int32, device=device)
+    scale = torch.tensor([.02, .05], device=device) if cache_dtype == torch.float8_e4m3fn else None
+    if paged:
+        kc = torch.zeros(B * cap // page, page, HK, D, dtype=cache_dtype, device=device)
+        table = torch.randperm(B * cap // page, generator=g).int().reshape(B, cap // page).to(device)
+        extra = dict(block_table=table)
+    else:
+        kc = torch.zeros(B + 1, cap, HK, D, dtype=cache_dtype, device=device)
+        extra = dict(cache_batch_idx=torch.tensor([2, 0, 3], dtype=torch.int32, device=device))
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    q_rot, k_rot = rotary(q, k, cos, sin, lengths, rotary_interleaved=interleaved, causal=causal)
+    append_kvcache(k_rot, v, kc, vc, lengths, k_scale=scale, v_scale=scale, **extra)
+    q_fused = rotary_append_kvcache(q, k, v, kc2, vc2, cos, sin, lengths, rotary_interleaved=interleaved,
+                                    causal=causal, k_scale=scale, v_scale=scale, **extra)
+    assert torch.equal(q_fused, q_rot)
+    assert torch.equal(kc2.view(torch.uint8), kc.view(torch.uint8))
+    assert torch.equal(vc2.view(torch.uint8), vc.view(torch.uint8))
