@@ -120,6 +120,12 @@ int validate(const fa_attention_args* a) {
                 "paged 4-D KV requires block_table; packed 3-D KV does not");
   FAB_CHECK_ARG(present(a->cu_seqlens_k) || present(a->seqused_k), "cu_seqlens_k or seqused_k is required");
   FAB_CHECK_ARG(a->num_splits >= 0, "num_splits must be nonnegative");
+  if (a->cp_world_size > 1) {
+    FAB_CHECK_ARG(a->cp_rank >= 0 && a->cp_rank < a->cp_world_size, "cp_rank must be in [0, cp_world_size)");
+    FAB_CHECK_ARG(present(a->cp_tot_seqused_k) && a->cp_tot_seqused_k.dtype == FA_I32 &&
+                      a->cp_tot_seqused_k.ndim == 1 && a->cp_tot_seqused_k.shape[0] == a->batch,
+                  "context parallelism needs cp_tot_seqused_k int32 [B]");
+  }
   FAB_CHECK_ARG(present(a->out) && a->out.ndim == 3 && a->out.shape[0] == q.shape[0] &&
                     a->out.shape[1] == heads && a->out.shape[2] == dv,
                 "out must have shape [total_q, query_heads, value_dim]");
@@ -194,6 +200,11 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
   descale(a->k_descale, &p->kd, &p->kd0, &p->kd1);
   descale(a->v_descale, &p->vd, &p->vd0, &p->vd1);
   p->mask = a->mask_kind; p->mask_win = a->mask_window; p->clamp = a->mask_clamp;
+  if (a->cp_world_size > 1) {
+    p->cp_n = a->cp_world_size; p->cp_r = a->cp_rank;
+    p->cp_tot = reinterpret_cast<const int32_t*>(a->cp_tot_seqused_k.ptr);
+    p->ct0 = a->cp_tot_seqused_k.stride[0];
+  }
   if (a->mask_kind == 1) {
     p->mr = reinterpret_cast<const int32_t*>(a->mask_aux0.ptr);
     p->mr0 = a->mask_aux0.stride[0]; p->mr1 = a->mask_aux0.stride[1];

@@ -44,7 +44,8 @@ __global__ void __launch_bounds__(kWarps * 32) generic_attention_kernel(AttnPara
                       (p.kd ? p.kd[b * p.kd0 + kh * p.kd1] : 1.f);
   const float vscale = p.vd ? p.vd[b * p.vd0 + kh * p.vd1] : 1.f;
   const float slope = p.alibi ? p.alibi[b * p.a0 + h * p.a1] : 0.f;
-  const float sink = (p.sinks && split == 0) ? load_float(p.sinks, p.sink_t, h * p.si0) : -INFINITY;
+  const float sink = (p.sinks && split == 0 && p.cp_r == 0) ? load_float(p.sinks, p.sink_t, h * p.si0) : -INFINITY;
+  const int k_tot = kv_total(p, b, k_len);  // global KV length (context parallelism)
 
   for (int z = tid; z < kRows * DQ; z += kWarps * 32) {
     const int r = z / DQ, d = z - r * DQ;
@@ -58,10 +59,12 @@ __global__ void __launch_bounds__(kWarps * 32) generic_attention_kernel(AttnPara
   int first = (int)((int64_t)tile_count * split / p.splits);
   int last = (int)((int64_t)tile_count * (split + 1) / p.splits);
   const int row_end = min(q_block + kRows, q_len);
-  if (causal && p.mask == 0) last = min(last, max(0, (row_end + k_len - q_len + kBK - 1) / kBK));
-  if (p.mask == 0 && p.win_l >= 0) first = max(first, max(0, q_block + k_len - q_len - p.win_l) / kBK);
-  if (p.mask == 0 && p.win_r >= 0)
-    last = min(last, max(0, (row_end + k_len - q_len + p.win_r + kBK - 1) / kBK));
+  if (p.cp_n <= 1) {  // tile skipping in local positions (positions are strided under context parallelism)
+    if (causal && p.mask == 0) last = min(last, max(0, (row_end + k_len - q_len + kBK - 1) / kBK));
+    if (p.mask == 0 && p.win_l >= 0) first = max(first, max(0, q_block + k_len - q_len - p.win_l) / kBK);
+    if (p.mask == 0 && p.win_r >= 0)
+      last = min(last, max(0, (row_end + k_len - q_len + p.win_r + kBK - 1) / kBK));
+  }
 
   float m[kRowsPerWarp], l[kRowsPerWarp], acc[kRowsPerWarp][NC];
 #pragma unroll
@@ -91,16 +94,16 @@ __global__ void __launch_bounds__(kWarps * 32) generic_attention_kernel(AttnPara
     for (int rr = 0; rr < kRowsPerWarp; ++rr) {
       const int r = warp * kRowsPerWarp + rr;
       if (q_block + r >= q_len) continue;
-      const int q_abs = q_block + r + k_len - q_len;
-      const int t = kb * kBK + lane;
+      const int q_abs = q_block + r + k_tot - q_len;
+      const int t = kb * kBK + lane, tg = key_pos(p, t);
       float dot = 0.f;
       const float* qrow = qs + r * DQ;
       const float* krow = ks + lane * LK;
       for (int d = 0; d < DQ; ++d) dot = fmaf(qrow[d], krow[d], dot);
       float s = dot * scale;
       if (p.softcap > 0.f) s = p.softcap * tanhf(s / p.softcap);
-      s -= slope * fabsf((float)(q_abs - t));
-      const bool keep = t < k_len && allowed_key(p, b, t, q_abs, (int64_t)q_begin + q_block + r, causal);
+      s -= slope * fabsf((float)(q_abs - tg));
+      const bool keep = t < k_len && allowed_key(p, b, tg, q_abs, (int64_t)q_begin + q_block + r, causal);
       s = keep ? s : -INFINITY;
       const float m_new = fmaxf(m[rr], warp_max(s));
       const float pr = (m_new == -INFINITY || s == -INFINITY) ? 0.f : expf(s - m_new);

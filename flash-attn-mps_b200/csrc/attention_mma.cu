@@ -107,16 +107,19 @@ __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParam
                       (p.kd ? p.kd[b * p.kd0 + kh * p.kd1] : 1.f);
   const float vscale = p.vd ? p.vd[b * p.vd0 + kh * p.vd1] : 1.f;
   const float slope = p.alibi ? p.alibi[b * p.a0 + h * p.a1] : 0.f;
-  const float sink = (p.sinks && split == 0) ? load_float(p.sinks, p.sink_t, h * p.si0) : -INFINITY;
+  const float sink = (p.sinks && split == 0 && p.cp_r == 0) ? load_float(p.sinks, p.sink_t, h * p.si0) : -INFINITY;
+  const int k_tot = kv_total(p, b, k_len);  // global KV length (context parallelism)
 
   // Tile bounds of this split (attention.metal:108-118, 64-key tiles).
   const int tile_count = (k_len + kBN - 1) / kBN;
   int first = (int)((int64_t)tile_count * split / p.splits);
   int last = (int)((int64_t)tile_count * (split + 1) / p.splits);
   const int row_end = min(q_block + kBM, q_len);
-  if (causal && p.mask == 0) last = min(last, max(0, (row_end + k_len - q_len + kBN - 1) / kBN));
-  if (p.mask == 0 && p.win_l >= 0) first = max(first, max(0, q_block + k_len - q_len - p.win_l) / kBN);
-  if (p.mask == 0 && p.win_r >= 0) last = min(last, max(0, (row_end + k_len - q_len + p.win_r + kBN - 1) / kBN));
+  if (p.cp_n <= 1) {  // tile skipping in local positions (positions are strided under context parallelism)
+    if (causal && p.mask == 0) last = min(last, max(0, (row_end + k_len - q_len + kBN - 1) / kBN));
+    if (p.mask == 0 && p.win_l >= 0) first = max(first, max(0, q_block + k_len - q_len - p.win_l) / kBN);
+    if (p.mask == 0 && p.win_r >= 0) last = min(last, max(0, (row_end + k_len - q_len + p.win_r + kBN - 1) / kBN));
+  }
 
   auto load_tile = [&](int kb, int st) {
     uint8_t* kdst = stage0 + st * L::kStageBytes;
@@ -262,12 +265,12 @@ __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParam
         for (int e = 0; e < 4; ++e) {
           const int row = e >> 1;
           const int q = q_block + warp * 16 + g + 8 * row;
-          const int t = kb * kBN + n * 8 + 2 * qd + (e & 1);
-          const int q_abs = q + k_len - q_len;
+          const int t = kb * kBN + n * 8 + 2 * qd + (e & 1), tg = key_pos(p, t);
+          const int q_abs = q + k_tot - q_len;
           float x = s[n][e] * scale;
           if (p.softcap > 0.f) x = p.softcap * tanhf(x / p.softcap);
-          x -= slope * fabsf((float)(q_abs - t));
-          const bool keep = q < q_len && t < k_len && allowed_key(p, b, t, q_abs, (int64_t)q_begin + q, causal);
+          x -= slope * fabsf((float)(q_abs - tg));
+          const bool keep = q < q_len && t < k_len && allowed_key(p, b, tg, q_abs, (int64_t)q_begin + q, causal);
           x = keep ? x * kLog2e : -INFINITY;
           s[n][e] = x;
           mx[row] = fmaxf(mx[row], x);
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kThreads) mma_attention_kernel(const AttnParam
 template <typename T, bool KV8, int DQ, int DV>
 int launch_shape(const AttnParams& p, cudaStream_t stream) {
   constexpr int smem = Layout<KV8, DQ, DV>::kSmem;
-  const bool simple = p.alibi == nullptr && p.softcap <= 0.f && p.mask == 0;
+  const bool simple = p.alibi == nullptr && p.softcap <= 0.f && p.mask == 0 && p.cp_n <= 1;
   auto kernel = p.ot == FA_F32 ? mma_attention_kernel<T, KV8, DQ, DV, true, false>
                 : simple       ? mma_attention_kernel<T, KV8, DQ, DV, false, true>
                                : mma_attention_kernel<T, KV8, DQ, DV, false, false>;

@@ -91,7 +91,13 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
   const int len = p.used ? p.used[b * p.u0] : p.cu_k[(b + 1) * p.ck0] - k_cu_begin;
   int left = p.leftpad ? p.leftpad[b * p.lp0] : 0;
   if (!p.paged) left += k_cu_begin;
-  const int visible_begin = p.win_l >= 0 ? max(0, len - p.win_l - 1) : 0;
+  // Left window in local positions; under context parallelism local key j is
+  // global j * cp_n + cp_r and the query is the last of cp_tot[b] tokens.
+  int visible_begin = p.win_l >= 0 ? max(0, len - p.win_l - 1) : 0;
+  if (p.cp_n > 1 && p.win_l >= 0) {
+    const int first_global = p.cp_tot[b * p.ct0] - 1 - p.win_l;  // smallest visible global position
+    visible_begin = max(0, (first_global - p.cp_r + p.cp_n - 1) / p.cp_n);
+  }
   const int begin = visible_begin + split * span;
   const int end = min(len, begin + span);
   const float qdesc = p.qd ? p.qd[b * p.qd0 + kh * p.qd1] : 1.f;
@@ -135,7 +141,7 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
       m[n8][c] = -INFINITY;
       l[n8][c] = 0.f;
       const int hcol = n8 * 8 + 2 * qd + c;
-      if (p.sinks && split == 0 && warp == 0 && hcol < nh) {
+      if (p.sinks && split == 0 && p.cp_r == 0 && warp == 0 && hcol < nh) {
         m[n8][c] = load_float(p.sinks, p.sink_t, (h0 + hcol) * p.si0) * kLog2e;
         l[n8][c] = g == 0 ? 1.f : 0.f;  // counted once across the column's lanes
       }

@@ -18,6 +18,13 @@ __device__ __forceinline__ int64_t kv_offset(const AttnParams& p, int b, int64_t
   return token * s1 + kh * s2;
 }
 
+// Global position of local key index t under context parallelism (identity
+// without it), and the global KV length the queries are aligned to.
+__device__ __forceinline__ int key_pos(const AttnParams& p, int t) { return p.cp_n > 1 ? t * p.cp_n + p.cp_r : t; }
+__device__ __forceinline__ int kv_total(const AttnParams& p, int b, int k_len) {
+  return p.cp_n > 1 ? p.cp_tot[b * p.ct0] : k_len;
+}
+
 // attention.metal:29-45
 __device__ __forceinline__ bool allowed_key(const AttnParams& p, int b, int token, int q_abs,
                                             int64_t packed_q, bool causal) {

@@ -51,6 +51,10 @@ struct AttnParams {
   const int32_t* mw;                      // mask kind 2 window [1]
   int64_t k_rows;                        // packed K/V: rows of the K/V tensors
   int64_t k_pages, bt_cols;              // paged K/V: pages in the cache, block_table columns
+  // Context parallelism: local key j is global position j * cp_n + cp_r;
+  // cp_tot[b] is the global KV length (queries sit at its end). cp_n <= 1: off.
+  const int32_t* cp_tot; int64_t ct0;
+  int32_t cp_n, cp_r;
   int32_t T, B, HQ, HK, DQ, DV, page;
   int32_t paged, causal, dynamic, win_l, win_r;
   int32_t mask, mask_win, clamp, splits, max_q, max_k;

@@ -838,7 +838,7 @@ int prefill_sm100_supported(const AttnParams& p) {
     for (int64_t v : ps)
       if (v <= 0 || (v * 2) % 16 != 0) return 0;
   }
-  if (p.alibi || p.mask || p.leftpad) return 0;
+  if (p.alibi || p.mask || p.leftpad || p.cp_n > 1) return 0;
   if (p.sinks && !(p.sink_t == FA_F32 || p.sink_t == FA_F16 || p.sink_t == FA_BF16)) return 0;
   if (p.qs2 != 1 || p.ks3 != 1 || p.vs3 != 1 || p.os2 != 1) return 0;
   if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !al16(p.out)) return 0;

@@ -37,7 +37,8 @@ def _i32(t, device):
 def build_args(q, k, v, out, lse, *, cu_seqlens_q, cu_seqlens_k, seqused_k, max_seqlen_q,
                max_seqlen_k, block_table, softmax_scale, causal, window_size, alibi_slopes,
                softcap, s_aux, q_descale, k_descale, v_descale, num_splits, mask_mod,
-               aux_tensors, leftpad_k, deterministic):
+               aux_tensors, leftpad_k, deterministic, cp_world_size=1, cp_rank=0,
+               cp_tot_seqused_k=None):
     """Fill the C argument struct; returns it plus the tensors it points into."""
     device = q.device
     keep = []
@@ -80,6 +81,9 @@ def build_args(q, k, v, out, lse, *, cu_seqlens_q, cu_seqlens_k, seqused_k, max_
     a.window_left, a.window_right = int(window_size[0]), int(window_size[1])
     a.num_splits = int(num_splits)
     a.deterministic = int(bool(deterministic))
+    if cp_world_size > 1:
+        a.cp_world_size, a.cp_rank = int(cp_world_size), int(cp_rank)
+        a.cp_tot_seqused_k = t(_i32(cp_tot_seqused_k, device))
     return a, keep
 
 
@@ -103,8 +107,15 @@ def attention(
     causal=False, window_size=(-1, -1), alibi_slopes=None, softcap=0.,
     s_aux=None, q_descale=None, k_descale=None, v_descale=None, out=None,
     num_splits=0, mask_mod=None, aux_tensors=None, leftpad_k=None, deterministic=False,
+    cp_world_size=1, cp_rank=0, cp_tot_seqused_k=None,
 ):
-    """Return packed output and natural-log LSE in ``[heads, total_q]`` order."""
+    """Return packed output and natural-log LSE in ``[heads, total_q]`` order.
+
+    ``cp_world_size > 1`` (context parallelism): k/v hold this rank's strided
+    share of every sequence (local key j = global position
+    j * cp_world_size + cp_rank), ``cp_tot_seqused_k`` the global KV lengths;
+    the result is this rank's partial state for an LSE merge across ranks.
+    """
     if q.device.type != "cuda" or k.device != q.device or v.device != q.device:
         raise ValueError("q, k and v must be on the same CUDA device")
     if q.ndim != 3 or k.ndim not in (3, 4) or v.ndim != k.ndim:
@@ -125,6 +136,12 @@ def attention(
         raise ValueError("cu_seqlens_k or seqused_k is required")
     if num_splits < 0:
         raise ValueError("num_splits must be nonnegative")
+    if cp_world_size > 1:
+        if not 0 <= cp_rank < cp_world_size:
+            raise ValueError("cp_rank must be in [0, cp_world_size)")
+        if (cp_tot_seqused_k is None or cp_tot_seqused_k.dtype != torch.int32 or cp_tot_seqused_k.ndim != 1
+                or cp_tot_seqused_k.numel() != cu_seqlens_q.numel() - 1 or cp_tot_seqused_k.device != q.device):
+            raise ValueError("context parallelism needs cp_tot_seqused_k as CUDA int32 [num_seqs]")
     out_dtype = torch.float16 if q.dtype == torch.float8_e4m3fn else q.dtype
     if out is None:
         out = torch.empty((tokens, heads, dv), dtype=out_dtype, device=q.device)
@@ -148,4 +165,5 @@ def attention(
                window_size=window_size, alibi_slopes=alibi_slopes, softcap=softcap,
                s_aux=s_aux, q_descale=q_descale, k_descale=k_descale, v_descale=v_descale,
                num_splits=num_splits, mask_mod=mask_mod, aux_tensors=aux_tensors,
-               leftpad_k=leftpad_k, deterministic=deterministic)
+               leftpad_k=leftpad_k, deterministic=deterministic, cp_world_size=cp_world_size,
+               cp_rank=cp_rank, cp_tot_seqused_k=cp_tot_seqused_k)

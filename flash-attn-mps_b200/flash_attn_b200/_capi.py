@@ -52,6 +52,9 @@ class AttentionArgs(ctypes.Structure):
         ("mask_clamp", ctypes.c_int32),
         ("num_splits", ctypes.c_int32),
         ("deterministic", ctypes.c_int32),
+        ("cp_tot_seqused_k", Tensor),
+        ("cp_world_size", ctypes.c_int32),
+        ("cp_rank", ctypes.c_int32),
     ]
 
 

@@ -131,7 +131,7 @@ def _run(q, k, v, *, cu_seqlens_q, cu_seqlens_k=None, seqused_k=None,
          causal=False, window_size=(-1, -1), alibi_slopes=None, softcap=0.0,
          s_aux=None, q_descale=None, k_descale=None, v_descale=None, out=None,
          num_splits=0, mask_mod=None, aux_tensors=None, leftpad_k=None,
-         deterministic=False):
+         deterministic=False, cp_world_size=1, cp_rank=0, cp_tot_seqused_k=None):
     """Validate everything, then run the packed attention core."""
     _inference_only(0, False, q, k, v, alibi_slopes, s_aux, q_descale, k_descale, v_descale, out)
     _validate(q, k, v, cu_seqlens_q, cu_seqlens_k, seqused_k, block_table, out)
@@ -147,7 +147,8 @@ def _run(q, k, v, *, cu_seqlens_q, cu_seqlens_k=None, seqused_k=None,
         alibi_slopes=alibi_slopes, softcap=softcap, s_aux=s_aux, q_descale=q_descale,
         k_descale=k_descale, v_descale=v_descale, out=out, num_splits=num_splits,
         mask_mod=mask_mod, aux_tensors=aux_tensors, leftpad_k=leftpad_k,
-        deterministic=deterministic)
+        deterministic=deterministic,
+        cp_world_size=cp_world_size, cp_rank=cp_rank, cp_tot_seqused_k=cp_tot_seqused_k)
 
 
 def flash_attn_varlen_func(

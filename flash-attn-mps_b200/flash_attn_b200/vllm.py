@@ -50,9 +50,16 @@ def flash_attn_varlen_func(
     _inference_only(dropout_p, return_attn_probs, q, k, v)
     if fa_version not in (2, 3, 4):
         raise ValueError("fa_version must be 2, 3, or 4")
-    if (q_v is not None or cp_world_size != 1 or cp_rank != 0
-            or cp_tot_seqused_k is not None or block_sparse_tensors is not None):
+    if q_v is not None or block_sparse_tensors is not None:
         raise NotImplementedError("MLA and separate sparse backends are outside the FLASH_ATTN contract")
+    # Context parallelism (vLLM DCP): this rank holds every cp_world_size-th KV
+    # token of each sequence starting at cp_rank; masks use global positions
+    # and the caller merges the ranks' (out, lse). The reference rejects these
+    # arguments (vllm.py:51-53).
+    if cp_world_size < 1 or (cp_world_size == 1 and (cp_rank != 0 or cp_tot_seqused_k is not None)):
+        raise ValueError("context parallelism needs cp_world_size > 1 with cp_rank and cp_tot_seqused_k")
+    if cp_world_size > 1 and cp_tot_seqused_k is None:
+        raise ValueError("context parallelism needs cp_tot_seqused_k (global KV lengths)")
     if output_scale is not None:
         raise NotImplementedError("vLLM FLASH_ATTN does not support fused output quantization")
     if aux_tensor_leading_dims is not None:
@@ -69,7 +76,8 @@ def flash_attn_varlen_func(
         alibi_slopes=alibi_slopes, softcap=softcap, s_aux=s_aux, q_descale=q_descale,
         k_descale=k_descale, v_descale=v_descale, out=out,
         num_splits=1 if deterministic else num_splits, mask_mod=mask_mod,
-        aux_tensors=aux_tensors, deterministic=deterministic or num_splits == 1)
+        aux_tensors=aux_tensors, deterministic=deterministic or num_splits == 1,
+        cp_world_size=cp_world_size, cp_rank=cp_rank, cp_tot_seqused_k=cp_tot_seqused_k)
     return (result, lse) if return_softmax_lse else result
 
 

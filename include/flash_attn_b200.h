@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define FA_B200_ABI_VERSION 1
+#define FA_B200_ABI_VERSION 2
 
 enum {
   FA_OK = 0,
@@ -94,6 +94,16 @@ typedef struct fa_attention_args {
   int32_t mask_clamp;       /* mm-prefix: clamp the bidirectional range to the window */
   int32_t num_splits;       /* 0 = library chooses; >0 exact split-KV count */
   int32_t deterministic;    /* 1 = fixed batch-invariant reduction schedule */
+  /* Context parallelism (vLLM DCP, ABI 2): this rank holds KV tokens
+   * cp_rank, cp_rank + cp_world_size, ... of each sequence (local index j =
+   * global position j * cp_world_size + cp_rank); causal, window, mask and
+   * ALiBi positions are global, queries sit at the end of cp_tot_seqused_k
+   * (int32 [B], the global KV lengths); sinks count on rank 0 only. The
+   * caller merges the ranks' (out, lse). cp_world_size 0 or 1 = off. No
+   * counterpart in the reference, which rejects these arguments
+   * (flash_attn_mps/vllm.py:51-53). */
+  fa_tensor cp_tot_seqused_k;
+  int32_t cp_world_size, cp_rank;
 } fa_attention_args;
 
 /* Library ABI version (FA_B200_ABI_VERSION). */

@@ -33,13 +33,15 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), f"{name} missing from the shared library"
     assert set(names) == set(_capi.SIGNATURES), "ctypes signatures out of sync with the header"
-    assert lib.fa_abi_version() == 1
+    assert lib.fa_abi_version() == 2
 
 
 def test_struct_layout_matches_header_order():
-    # 19 tensor descriptors (80 bytes each) then 13 4-byte scalars, padded to 8.
+    # 19 tensor descriptors (80 bytes each), 13 4-byte scalars, then (ABI 2)
+    # one more descriptor (8-byte aligned) and 2 scalars.
     assert ctypes.sizeof(_capi.Tensor) == 8 + 4 + 4 + 32 + 32
-    assert ctypes.sizeof(_capi.AttentionArgs) == (19 * 80 + 13 * 4 + 7) // 8 * 8
+    head = (19 * 80 + 13 * 4 + 7) // 8 * 8
+    assert ctypes.sizeof(_capi.AttentionArgs) == head + 80 + 8
 
 
 def test_invalid_arguments_are_reported_without_a_gpu():
@@ -67,8 +69,10 @@ def test_vllm_rejections_precede_launch():
                 cu_seqlens_k=cu)
     with pytest.raises(ValueError, match="fa_version"):
         fvllm.flash_attn_varlen_func(**base, fa_version=5)
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="cp_tot_seqused_k"):
         fvllm.flash_attn_varlen_func(**base, cp_world_size=2)
+    with pytest.raises(NotImplementedError):
+        fvllm.flash_attn_varlen_func(**base, q_v=q)
     with pytest.raises(NotImplementedError):
         fvllm.flash_attn_varlen_func(**base, output_scale=torch.ones(1))
     with pytest.raises(ValueError):
