@@ -16,7 +16,8 @@ with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
 that token, attention, D2H of the output.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_decode|prefill|prefill_softcap_window|bf16_decode] [--small]
+                    [--workload fp8_decode|prefill|prefill_softcap_window|bf16_decode|serving]
+                    [--attention-path fused|native] [--small]
 """
 
 import argparse
@@ -238,11 +239,14 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
+    from flash_attn_b200._capi import kernel_launches
+    launches_before = kernel_launches()
     start.record(stream)
     for _ in range(args.steps):
         step(q)
     end.record(stream)
     barrier(world)
+    launches = kernel_launches() - launches_before
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms, world)
 
@@ -314,7 +318,7 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
                    "head_dim": D, "kv_bytes_total": B * C * HK * 2 * D,
                    "l2": "inputs (17.2 GB cache) larger than L2; no flush needed",
                    "parallelism": f"kv-seq sharded x{world} + NCCL all-gather + merge"},
-        "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "gpu_launches": launches,
         "clocks": clocks,
     }
     return result
@@ -428,6 +432,157 @@ def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False):
                          "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)"}}
 
 
+# ------------------------------------------------------- config 5 (N=1)
+CFG5 = dict(requests=64, prompt=1024, decode_steps=256, seed=5)
+
+
+def _graph_ms(fn, reps, warmup=2):
+    """Device time of ``fn`` captured as one CUDA graph, per replay."""
+    import torch
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    ms = time_loop(graph.replay, reps, warmup)
+    del graph
+    return ms
+
+
+def cpu_serving_sample(prompt=256, decode_steps=16, seed=5):
+    """The reference's frozen SDPA engine path (oracle) on host cores: 1 request."""
+    import torch
+    from oracle.engine_sdpa import SdpaAttention
+    from serving_loop import Engine, Qwen3Shape, init_weights
+    shape = Qwen3Shape()
+    cpu = torch.device("cpu")
+    weights = init_weights(shape, cpu, seed=seed)
+    engine = Engine(shape, weights, SdpaAttention, 1, prompt + decode_steps + 1, cpu, seed=seed)
+    tokens = torch.randint(0, shape.vocab, (prompt,), generator=torch.Generator().manual_seed(seed))
+    t0 = time.perf_counter()
+    logits, start = engine.prefill([tokens])
+    for _ in range(decode_steps):
+        logits = engine.decode(logits.argmax(dim=-1), start)
+        start = start + 1
+    dt = time.perf_counter() - t0
+    return {"value": (decode_steps + 1) / dt, "unit": "output tokens/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds": dt,
+            "sample": f"1 request: {prompt}-token prompt + {decode_steps} greedy decode steps, full 28-layer "
+                      f"model, torch CPU GEMMs + float64 SDPA attention (the reference's frozen SDPA path)"}
+
+
+def run_serving(peaks, peak_kind, steps=2, warmup=3, small=False, path="fused", cpu_baseline=False):
+    """Config 5: Qwen3-0.6B-shaped serving loop, attention through the library.
+
+    One step = prefill of every prompt (eager) + ``decode_steps`` greedy decode
+    steps (one CUDA graph replay each). value = output tokens / s (the first
+    token comes from the prefill); attention's share is measured by timing the
+    28 layers' attention calls alone, captured in graphs, for the prefill step
+    and for a decode step at the mid-loop position.
+    """
+    import torch
+    from flash_attn_b200._capi import kernel_launches
+    from serving_loop import (DecodeGraph, Engine, FusedAttention, NativeAttention, Qwen3Shape,
+                              decode_step, init_weights, prefill_step)
+    cfg = dict(CFG5)
+    if small:
+        cfg.update(requests=8, prompt=256, decode_steps=16)
+    B, S, N = cfg["requests"], cfg["prompt"], cfg["decode_steps"]
+    shape = Qwen3Shape()
+    dev = torch.device("cuda")
+    weights = init_weights(shape, dev, seed=cfg["seed"])
+    backend = FusedAttention if path == "fused" else NativeAttention
+    engine = Engine(shape, weights, backend, B, S + N + 1, dev, seed=cfg["seed"])
+    prompts_host = torch.randint(0, shape.vocab, (B, S),
+                                 generator=torch.Generator().manual_seed(cfg["seed"])).pin_memory()
+    prompts = prompts_host.to(dev)
+    history = torch.zeros(B, N + 1, dtype=torch.long, device=dev)
+    history_host = torch.empty(B, N + 1, dtype=torch.long).pin_memory()
+
+    c0 = kernel_launches()
+    logits, start = engine.prefill(list(prompts.unbind(0)))
+    prefill_launches = kernel_launches() - c0
+    c0 = kernel_launches()
+    graph = DecodeGraph(engine, logits.argmax(dim=-1), start.clone(), history)
+    decode_launches = (kernel_launches() - c0) // 2  # one eager warm-up + one capture
+
+    def loop(src):
+        logits, start = engine.prefill(list(src.unbind(0)))
+        first = logits.argmax(dim=-1)
+        history[:, 0].copy_(first)
+        graph.reset(first, start, col=1)
+        for _ in range(N):
+            graph.replay()
+
+    for _ in range(warmup):
+        loop(prompts)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
+    time.sleep(0.3)
+    ms = time_loop(lambda: loop(prompts), steps, 0)
+    prefill_ms = time_loop(lambda: engine.prefill(list(prompts.unbind(0))), steps, 1)
+    clocks = sampler.stop()
+
+    def e2e_loop():
+        prompts.copy_(prompts_host, non_blocking=True)
+        loop(prompts)
+        history_host.copy_(history, non_blocking=True)
+
+    e2e_ms = time_loop(e2e_loop, steps, 1)
+
+    # Attention alone: the 28 layers' calls on the prefill step and on one decode step.
+    g = torch.Generator(device=dev).manual_seed(7)
+    T = B * S
+    q = torch.randn(T, shape.heads, shape.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(T, shape.kv_heads, shape.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    pstep = prefill_step(engine.cache, [S] * B, shape.page, dev)
+    dstart = torch.full((B,), S + N // 2, dtype=torch.int32, device=dev)
+    dstep = decode_step(engine.cache, dstart, shape.page)
+
+    def layers_attention(step, rows):
+        for i in range(shape.layers):  # outputs die each iteration: the graph pool reuses them
+            engine.backend(i, q[:rows], k[:rows], v[:rows], step)
+
+    attn_prefill_ms = _graph_ms(lambda: layers_attention(pstep, T), 3)
+    attn_decode_ms = _graph_ms(lambda: layers_attention(dstep, B), 20)
+    decode_step_ms = (ms - prefill_ms) / N
+    del q, k, v
+
+    out_tokens = B * (N + 1)
+    flops = shape.layers * shape.heads * 4 * shape.head_dim * B * S * (S + 1) // 2
+    tflops = flops / (attn_prefill_ms * 1e-3) / 1e12
+    line = {
+        "value": out_tokens / (ms * 1e-3), "unit": "output tokens/s", "ms_per_step": ms,
+        "workload": f"cfg5: Qwen3-0.6B-shaped serving loop, random bf16 weights, {B} requests x {S}-token "
+                    f"prompts (prefill) + {N} greedy decode steps (CUDA graph), page 16, "
+                    f"attention path '{path}'" + (" (small profiling case)" if small else ""),
+        "prefill_ms": prefill_ms, "decode_step_ms": decode_step_ms,
+        "attention": {"prefill_ms": attn_prefill_ms, "prefill_share": attn_prefill_ms / prefill_ms,
+                      "decode_step_ms": attn_decode_ms, "decode_share": attn_decode_ms / decode_step_ms,
+                      "prefill_attention_tflop": flops / 1e12},
+        "e2e": {"value": out_tokens / (e2e_ms * 1e-3), "unit": "output tokens/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": prompts_host.numel() * 8, "d2h_bytes_per_step": history_host.numel() * 8},
+        "roofline": {"bound": "tensor", "kernel": "prefill_sm100_kernel (28 layers' prefill attention"
+                     + (", with the fused RoPE+append launches)" if path == "fused" else ", with store_kvcache)"),
+                     "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / peaks["bf16_tflops"], "peak_kind": f"{peak_kind} (bf16_tflops, burst)",
+                     "traffic": None},
+        "gpu_launches": steps * (prefill_launches + N * decode_launches),
+        "clocks": clocks,
+    }
+    del graph, engine, weights
+    torch.cuda.empty_cache()
+    if cpu_baseline:
+        line["cpu_baseline"] = cpu_serving_sample()
+    return line
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_fp8_decode_sample(cfg, requests=1, seed=4):
     """The oracle (reference CPU math, float64) on a bounded sample of config 4."""
@@ -494,8 +649,11 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "bf16_decode"],
+    ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "bf16_decode",
+                                           "serving"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
+    ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
+                    help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
     ap.add_argument("--small", action="store_true", help="shrunken workload for ncu captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-2/3 measurements")
@@ -516,6 +674,18 @@ def main():
             if args.workload == "prefill":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small)
                 value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload == "serving":
+                # One step is a whole serving loop (~0.5 s): at most 5 timed loops.
+                steps = min(args.steps, 5)
+                r = run_serving(peaks, peak_kind, steps=steps, warmup=args.warmup, small=args.small,
+                                path=args.attention_path, cpu_baseline=not args.no_cpu_baseline and not args.small)
+                r["config"] = {"workload": r.pop("workload"),
+                               "l2": "weights (1.2 GB) and paged caches (9.5 GB) larger than L2; no flush"}
+                r.update({"metric": METRIC, "n_gpus": 1, "steps": steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "bf16", "data": "synthetic (seeded random weights and prompts)"})
+                print(json.dumps(r))
+                return
             elif args.workload == "prefill_softcap_window":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, softcap=50.0,
                                 window=(1024, 0), small=args.small)
@@ -541,7 +711,8 @@ def main():
             line["secondary"] = {"prefill_cfg2": run_prefill(peaks, peak_kind),
                                  "prefill_cfg2_softcap_window": run_prefill(peaks, peak_kind, softcap=50.0,
                                                                             window=(1024, 0)),
-                                 "decode_cfg3": run_bf16_decode(peaks, peak_kind)}
+                                 "decode_cfg3": run_bf16_decode(peaks, peak_kind),
+                                 "serving_cfg5": run_serving(peaks, peak_kind)}
         if world == 1 and not args.no_cpu_baseline and not args.small:
             line["cpu_baseline"] = cpu_baseline_block(CFG4)
         print(json.dumps(line))

@@ -13,6 +13,7 @@
 // tensor values or lengths beyond the caller's max_seqlen_*.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -290,6 +291,13 @@ using namespace fab;
 extern "C" int fa_abi_version(void) { return FA_B200_ABI_VERSION; }
 
 extern "C" const char* fa_last_error(void) { return last_error().c_str(); }
+
+namespace fab {
+static std::atomic<unsigned long long> g_kernel_launches{0};
+void note_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace fab
+
+extern "C" uint64_t fa_kernel_launches(void) { return fab::g_kernel_launches.load(std::memory_order_relaxed); }
 
 extern "C" int fa_pipeline_timeouts(int clear) {
   const int a = fab::prefill_timeout_flag(clear != 0);

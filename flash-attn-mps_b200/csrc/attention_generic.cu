@@ -161,6 +161,7 @@ int launch_nc(const AttnParams& p, cudaStream_t stream) {
   }
   dim3 grid((unsigned)((p.max_q + kRows - 1) / kRows), (unsigned)p.HQ, (unsigned)((int64_t)p.B * p.splits));
   kernel<<<grid, kWarps * 32, smem, stream>>>(p);
+  note_launch();
   FAB_LAUNCH_CHECK("generic attention launch");
   return FA_OK;
 }

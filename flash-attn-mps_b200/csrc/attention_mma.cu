@@ -381,6 +381,7 @@ int launch_shape(const AttnParams& p, cudaStream_t stream) {
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "mma attention smem attribute: %s", cudaGetErrorString(e));
   dim3 grid((unsigned)((p.max_q + kBM - 1) / kBM), (unsigned)p.HQ, (unsigned)((int64_t)p.B * p.splits));
   kernel<<<grid, kThreads, smem, stream>>>(p);
+  note_launch();
   FAB_LAUNCH_CHECK("mma attention launch");
   return FA_OK;
 }

@@ -247,6 +247,7 @@ void launch_store(const StoreArgs& a, bool vec, int sides, cudaStream_t stream) 
   dim3 grid((unsigned)blocks, (unsigned)sides), block((unsigned)bx, (unsigned)by);
   if (vec) store_kernel<T, FP8, Vec16<T>::N><<<grid, block, 0, stream>>>(a);
   else store_kernel<T, FP8, 1><<<grid, block, 0, stream>>>(a);
+  note_launch();
 }
 
 int dispatch_store(const StoreArgs& a, int dtype, bool fp8, bool vec, int sides, cudaStream_t st) {
@@ -447,6 +448,236 @@ int grid_for(int64_t units) {
   return (int)(blocks < 1 ? 1 : blocks);
 }
 
+// ------------------------------------------- vectorized RoPE + append
+// The same element values as append_kernel / rotary_append_kernel (identical
+// mul/add roundings, same skips) for 16-bit rows with unit inner stride:
+// each thread moves one 16-byte vector of 8 elements of one head row, and a
+// split-half rotation pairs the vector at e with the one at e + half. Sides:
+// blockIdx.y 0 = K (rotated when `rotate`), 1 = V, 2 = Q (rotated into q_out).
+struct VecSide {
+  const uint8_t* x; uint8_t* dst;  // byte pointers (dst: cache, or q_out for Q)
+  int64_t xs0, xs1, xs2;           // element strides of x [B,S,H,D]
+  int64_t ds0, ds1, ds2;           // cache [N|rows, P|cap, H, D], or q_out [B,S,H,D]
+  const float* scale; int64_t scale_stride;
+  int32_t H, V, fp8, rotate;       // V = D / 8
+};
+
+struct VecArgs {
+  VecSide side[3];
+  const float* cos; const float* sin; int64_t cs0, ss0;
+  int32_t half, interleaved, advance_q;
+  const int32_t* lengths; int64_t len_stride;
+  const int32_t* batch_idx; int64_t bi_stride;
+  const int32_t* table; int64_t bt0, bt1;
+  int32_t paged, pages_per_seq, P, remap, S;
+  int64_t blocks, rows, tokens;
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+      f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    } else {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = t.x; f[2 * i + 1] = t.y;
+    }
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      const __nv_bfloat162 t = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&t);
+    } else {
+      const __half2 t = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t*>(&t);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Store 8 values at element e of a destination row: RN to T, or (FP8 cache)
+// the saturating E4M3 code of float(T-rounded value) / scale.
+template <typename T>
+__device__ __forceinline__ void put8(const VecSide& s, uint8_t* row, int e, const float (&f)[8], float scale) {
+  if (!s.fp8) {
+    *reinterpret_cast<uint4*>(row + (int64_t)e * sizeof(T)) = pack8<T>(f);
+    return;
+  }
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v = std::is_same<T, __nv_bfloat16>::value ? __bfloat162float(__float2bfloat16_rn(f[i]))
+                                                           : __half2float(__float2half_rn(f[i]));
+    w[i >> 2] |= (uint32_t)float_to_e4m3_sat(__fdiv_rn(v, scale)) << ((i & 3) * 8);
+  }
+  *reinterpret_cast<uint2*>(row + e) = make_uint2(w[0], w[1]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) rope_append_vec_kernel(VecArgs a) {
+  const int which = blockIdx.y;
+  const VecSide& s = a.side[which];
+  if (s.x == nullptr) return;
+  const int units = s.H * s.V;
+  const int64_t total = a.tokens * units;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
+    int64_t tok;
+    int u;
+    if (total <= 0x7fffffff) {
+      const uint32_t ee = (uint32_t)e;
+      tok = ee / (uint32_t)units;
+      u = (int)(ee - (uint32_t)tok * (uint32_t)units);
+    } else {
+      tok = e / units;
+      u = (int)(e - tok * units);
+    }
+    const int h = u / s.V;
+    const int c0 = (u - h * s.V) * 8;
+    const int64_t b = tok / a.S;
+    const int j = (int)(tok - b * a.S);
+    const int64_t len = a.lengths[b * a.len_stride];
+    int64_t pos;
+    uint8_t* out;
+    if (which == 2) {
+      pos = len + (a.advance_q ? j : 0);
+      out = s.dst + (b * s.ds0 + j * s.ds1 + h * s.ds2) * (int64_t)sizeof(T);
+    } else {
+      pos = len + j;
+      const int64_t row = a.remap ? (int64_t)a.batch_idx[b * a.bi_stride] : b;
+      const int64_t capacity = a.paged ? (int64_t)a.pages_per_seq * a.P : a.P;
+      if (row < 0 || row >= a.rows || pos < 0 || pos >= capacity) continue;
+      const int64_t block = a.paged ? (int64_t)a.table[row * a.bt0 + (pos / a.P) * a.bt1] : row;
+      if (block < 0 || block >= a.blocks) continue;
+      const int64_t offset = a.paged ? pos % a.P : pos;
+      out = s.dst + (block * s.ds0 + offset * s.ds1 + h * s.ds2) * (int64_t)(s.fp8 ? 1 : sizeof(T));
+    }
+    const uint8_t* in = s.x + (b * s.xs0 + j * s.xs1 + h * s.xs2) * (int64_t)sizeof(T);
+    const float scale = s.fp8 && s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+    const bool rotated = s.rotate && c0 < 2 * a.half;
+    if (!rotated) {
+      if (!s.fp8) {
+        *reinterpret_cast<uint4*>(out + (int64_t)c0 * sizeof(T)) =
+            __ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T)));
+      } else {
+        float f[8];
+        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), f);
+        put8<T>(s, out, c0, f, scale);
+      }
+      continue;
+    }
+    if (a.interleaved) {
+      // Pairs (c0 + 2k, c0 + 2k + 1) use angle index c0/2 + k.
+      float x[8], o[8];
+      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x);
+      const float4 cv = __ldg(reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0 / 2));
+      const float4 sv = __ldg(reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0 / 2));
+      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[2 * k] = __fadd_rn(__fmul_rn(x[2 * k], cc[k]), -__fmul_rn(x[2 * k + 1], ss[k]));
+        o[2 * k + 1] = __fadd_rn(__fmul_rn(x[2 * k + 1], cc[k]), __fmul_rn(x[2 * k], ss[k]));
+      }
+      put8<T>(s, out, c0, o, scale);
+    } else {
+      if (c0 >= a.half) continue;  // the partner vector at c0 - half writes this one
+      float x1[8], x2[8], o1[8], o2[8];
+      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x1);
+      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)(c0 + a.half) * sizeof(T))), x2);
+      const float4* cp = reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0);
+      const float4* sp = reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0);
+      const float4 ca = __ldg(cp), cb = __ldg(cp + 1), sa = __ldg(sp), sb = __ldg(sp + 1);
+      const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+      const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        o1[k] = __fadd_rn(__fmul_rn(x1[k], cc[k]), -__fmul_rn(x2[k], ss[k]));
+        o2[k] = __fadd_rn(__fmul_rn(x2[k], cc[k]), __fmul_rn(x1[k], ss[k]));
+      }
+      put8<T>(s, out, c0, o1, scale);
+      put8<T>(s, out, c0 + a.half, o2, scale);
+    }
+  }
+}
+
+inline bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+// Launch the vectorized kernel when every operand qualifies; returns 1 when it
+// did not apply (the caller runs the scalar kernel), else FA_OK / an error.
+// `r` may be null (plain append, nothing rotated).
+int launch_rope_append_vec(const AppendArgs& a, const RopeArgs* r, int64_t batch, cudaStream_t stream) {
+  int dtype = -1;
+  VecArgs v{};
+  bool any = false;
+  for (int i = 0; i < 2; ++i) {
+    const AppendSide& s = a.side[i];
+    if (!s.x) continue;
+    if (s.xdtype != FA_BF16 && s.xdtype != FA_F16) return 1;
+    if (dtype >= 0 && s.xdtype != dtype) return 1;
+    dtype = s.xdtype;
+    if (s.D % 8 || s.xs3 != 1 || s.cs3 != 1) return 1;
+    if (s.xs0 % 8 || s.xs1 % 8 || s.xs2 % 8 || !aligned(s.x, 16)) return 1;
+    if (s.cs0 % 8 || s.cs1 % 8 || s.cs2 % 8 || !aligned(s.cache, s.fp8 ? 8 : 16)) return 1;
+    if (v.S && v.S != s.S) return 1;
+    v.S = s.S;
+    VecSide& o = v.side[i];
+    o.x = reinterpret_cast<const uint8_t*>(s.x); o.dst = reinterpret_cast<uint8_t*>(s.cache);
+    o.xs0 = s.xs0; o.xs1 = s.xs1; o.xs2 = s.xs2; o.ds0 = s.cs0; o.ds1 = s.cs1; o.ds2 = s.cs2;
+    o.scale = s.scale; o.scale_stride = s.scale_stride;
+    o.H = s.H; o.V = s.D / 8; o.fp8 = s.fp8; o.rotate = (r != nullptr && i == 0);
+    any = true;
+  }
+  int sides = 2;
+  if (r) {
+    if (r->cdtype != FA_F32 || r->cs1 != 1 || r->ss1 != 1 || r->cs0 % 4 || r->ss0 % 4) return 1;
+    if (!aligned(r->cos, 16) || !aligned(r->sin, 16)) return 1;
+    if (r->interleaved ? (r->half % 4) : (r->half % 8)) return 1;
+    v.cos = reinterpret_cast<const float*>(r->cos); v.sin = reinterpret_cast<const float*>(r->sin);
+    v.cs0 = r->cs0; v.ss0 = r->ss0;
+    v.half = r->half; v.interleaved = r->interleaved; v.advance_q = r->advance_q;
+    if (r->q) {
+      if (r->qdtype != dtype || r->QD % 8 || r->qs3 != 1 || r->qo3 != 1) return 1;
+      if (r->qs0 % 8 || r->qs1 % 8 || r->qs2 % 8 || r->qo0 % 8 || r->qo1 % 8 || r->qo2 % 8) return 1;
+      if (!aligned(r->q, 16) || !aligned(r->q_out, 16) || (v.S && r->QS != v.S)) return 1;
+      VecSide& o = v.side[2];
+      o.x = reinterpret_cast<const uint8_t*>(r->q); o.dst = reinterpret_cast<uint8_t*>(r->q_out);
+      o.xs0 = r->qs0; o.xs1 = r->qs1; o.xs2 = r->qs2; o.ds0 = r->qo0; o.ds1 = r->qo1; o.ds2 = r->qo2;
+      o.H = r->QH; o.V = r->QD / 8; o.rotate = 1;
+      v.S = r->QS;
+      sides = 3;
+      any = true;
+    }
+  }
+  if (!any || dtype < 0) return 1;
+  v.lengths = a.lengths; v.len_stride = a.len_stride;
+  v.batch_idx = a.batch_idx; v.bi_stride = a.bi_stride;
+  v.table = a.table; v.bt0 = a.bt0; v.bt1 = a.bt1;
+  v.paged = a.paged; v.pages_per_seq = a.pages_per_seq; v.P = a.P; v.remap = a.remap;
+  v.blocks = a.blocks; v.rows = a.rows; v.tokens = batch * v.S;
+  int64_t vectors = 0;
+  for (int i = 0; i < 3; ++i)
+    if (v.side[i].x) {
+      const int64_t n = v.tokens * v.side[i].H * v.side[i].V;
+      vectors = n > vectors ? n : vectors;
+    }
+  if (vectors == 0) return FA_OK;
+  const dim3 grid(grid_for(vectors), sides);
+  if (dtype == FA_BF16) rope_append_vec_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(v);
+  else rope_append_vec_kernel<__half><<<grid, 256, 0, stream>>>(v);
+  note_launch();
+  FAB_LAUNCH_CHECK("vectorized append launch");
+  return FA_OK;
+}
+
 int prepare_append_side(const fa_tensor* x, const fa_tensor* cache, const fa_tensor* scale,
                         int64_t batch, AppendSide* s) {
   s->x = nullptr;
@@ -562,6 +793,8 @@ extern "C" int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
       units = n > units ? n : units;
     }
   if (units == 0) return FA_OK;
+  const int vrc = launch_rope_append_vec(a, nullptr, batch, reinterpret_cast<cudaStream_t>(stream));
+  if (vrc != 1) return vrc;
   // Each side iterates over its own element count; the shorter one exits early.
   a.units = units;
   AppendArgs per[2] = {a, a};
@@ -572,6 +805,7 @@ extern "C" int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
     per[i].units = batch * a.side[i].S * (int64_t)a.side[i].H * a.side[i].D;
     if (per[i].units == 0) continue;
     append_kernel<<<dim3(grid_for(per[i].units), 1), 256, 0, st>>>(per[i]);
+    note_launch();
     FAB_LAUNCH_CHECK("append_kvcache launch");
   }
   return FA_OK;
@@ -647,7 +881,10 @@ extern "C" int fa_rotary_append_kvcache(const fa_tensor* q, const fa_tensor* q_o
     sides = 3;
   }
   if (units == 0) return FA_OK;
+  const int vrc = launch_rope_append_vec(a, &r, batch, reinterpret_cast<cudaStream_t>(stream));
+  if (vrc != 1) return vrc;
   rotary_append_kernel<<<dim3(grid_for(units), sides), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, r);
+  note_launch();
   FAB_LAUNCH_CHECK("rotary append launch");
   return FA_OK;
 }
@@ -680,6 +917,7 @@ extern "C" int fa_rotary(const fa_tensor* x, const fa_tensor* out, const fa_tens
   a.units = x->shape[0] * x->shape[1] * x->shape[2] * x->shape[3];
   if (a.units == 0) return FA_OK;
   rotary_kernel<<<grid_for(a.units), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  note_launch();
   FAB_LAUNCH_CHECK("rotary launch");
   return FA_OK;
 }

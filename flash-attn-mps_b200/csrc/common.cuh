@@ -105,4 +105,8 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Host-side count of kernel launches issued by the library; every launch
+// site calls this right after its <<<...>>> (defined in attention.cu).
+void note_launch();
+
 }  // namespace fab

@@ -619,6 +619,7 @@ int launch_cfg(const AttnParams& p, int splits, int span, cudaStream_t stream) {
   }
   dim3 grid((unsigned)splits, (unsigned)(p.HK * hblocks), (unsigned)p.B);
   kernel<<<grid, (W + (tma ? 1 : 0)) * 32, smem, stream>>>(tmk, tmv, p, span, hblocks, shift, box_tok);
+  note_launch();
   FAB_LAUNCH_CHECK("decode launch");
   return FA_OK;
 }

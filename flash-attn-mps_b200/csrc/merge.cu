@@ -107,6 +107,7 @@ int launch_merge_partials(const MergePartialsArgs& a, cudaStream_t stream) {
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
   merge_partials_kernel<<<(unsigned)blocks, 256, 0, stream>>>(a);
+  note_launch();
   FAB_LAUNCH_CHECK("merge_partials launch");
   return FA_OK;
 }
@@ -155,6 +156,7 @@ extern "C" int fa_merge_attn_states(const fa_tensor* out, const fa_tensor* left,
   const int64_t cap = (int64_t)sm_count() * 8;
   if (blocks > cap) blocks = cap;
   merge_pair_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  note_launch();
   FAB_LAUNCH_CHECK("merge_attn_states launch");
   return FA_OK;
 }

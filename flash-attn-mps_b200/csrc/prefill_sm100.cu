@@ -930,6 +930,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   e = cudaMemsetAsync(pp.counter, 0, sizeof(int), stream);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill counter reset: %s", cudaGetErrorString(e));
   kernel<<<grid, kThreads, kSmemBytes, stream>>>(mq, mk, mv, mo, pp);
+  note_launch();
   FAB_LAUNCH_CHECK("prefill launch");
   return FA_OK;
 }

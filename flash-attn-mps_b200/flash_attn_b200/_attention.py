@@ -107,9 +107,12 @@ def attention(
     causal=False, window_size=(-1, -1), alibi_slopes=None, softcap=0.,
     s_aux=None, q_descale=None, k_descale=None, v_descale=None, out=None,
     num_splits=0, mask_mod=None, aux_tensors=None, leftpad_k=None, deterministic=False,
-    cp_world_size=1, cp_rank=0, cp_tot_seqused_k=None,
+    cp_world_size=1, cp_rank=0, cp_tot_seqused_k=None, lse=None,
 ):
     """Return packed output and natural-log LSE in ``[heads, total_q]`` order.
+
+    ``out`` and ``lse`` (fp32 ``[heads, total_q]``, any strides) may be given
+    to receive the result in place.
 
     ``cp_world_size > 1`` (context parallelism): k/v hold this rank's strided
     share of every sequence (local key j = global position
@@ -158,7 +161,10 @@ def attention(
     if max_seqlen_q == 1 and tokens > cu_seqlens_q.numel() - 1:
         # reference _decode.py:54-55
         raise ValueError("decode accepts at most one query per request")
-    lse = torch.empty((heads, tokens), device=q.device, dtype=torch.float32)
+    if lse is None:
+        lse = torch.empty((heads, tokens), device=q.device, dtype=torch.float32)
+    elif tuple(lse.shape) != (heads, tokens) or lse.dtype != torch.float32 or lse.device != q.device:
+        raise ValueError("lse must be CUDA float32 [query_heads, total_q]")
     return run(q, k, v, out, lse, cu_seqlens_q=cu_seqlens_q, cu_seqlens_k=cu_seqlens_k,
                seqused_k=seqused_k, max_seqlen_q=max_seqlen_q, max_seqlen_k=max_seqlen_k,
                block_table=block_table, softmax_scale=softmax_scale, causal=causal,

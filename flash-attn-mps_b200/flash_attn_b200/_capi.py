@@ -60,10 +60,13 @@ class AttentionArgs(ctypes.Structure):
 
 _P = ctypes.POINTER
 # (name, argtypes) of every exported entry point; tests check the header too.
+_RESTYPES = {"fa_last_error": ctypes.c_char_p, "fa_kernel_launches": ctypes.c_uint64}
+
 SIGNATURES = {
     "fa_abi_version": [],
     "fa_last_error": [],
     "fa_pipeline_timeouts": [ctypes.c_int],
+    "fa_kernel_launches": [],
     "fa_attention_workspace_size": [_P(AttentionArgs), _P(ctypes.c_size_t)],
     "fa_attention_fwd": [_P(AttentionArgs), ctypes.c_void_p],
     "fa_decode_fwd_noalloc": [_P(AttentionArgs), ctypes.c_void_p],
@@ -93,9 +96,14 @@ def library():
                 for name, argtypes in SIGNATURES.items():
                     fn = getattr(lib, name)
                     fn.argtypes = argtypes
-                    fn.restype = ctypes.c_char_p if name == "fa_last_error" else ctypes.c_int
+                    fn.restype = _RESTYPES.get(name, ctypes.c_int)
                 _lib = lib
     return _lib
+
+
+def kernel_launches():
+    """Kernel launches the library has issued so far (graph replays not counted)."""
+    return int(library().fa_kernel_launches())
 
 
 def tensor(t, dtype_override=None):

@@ -125,6 +125,15 @@ const char* fa_last_error(void);
 int fa_pipeline_timeouts(int clear);
 
 /*
+ * Kernel launches this library has issued in the process so far: a host-side
+ * counter incremented at every launch site. A launch recorded into a CUDA
+ * graph counts once, at capture, not per replay. A diagnostic for benchmarks
+ * (how many of the library's kernels a timed region ran); no counterpart in
+ * the reference.
+ */
+uint64_t fa_kernel_launches(void);
+
+/*
  * Bytes of device workspace fa_attention_fwd needs for these arguments
  * (split-KV partial outputs and LSEs). Host-only; reads no tensor values.
  * Replaces the partial-buffer allocation of flash_attn_mps/_attention.py:244-249

@@ -34,6 +34,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), f"{name} missing from the shared library"
     assert set(names) == set(_capi.SIGNATURES), "ctypes signatures out of sync with the header"
     assert lib.fa_abi_version() == 2
+    assert _capi.kernel_launches() >= 0
 
 
 def test_struct_layout_matches_header_order():

@@ -222,3 +222,47 @@ def test_fused_rotary_append_equals_rotary_then_append(device, cache_dtype, page
     assert torch.equal(q_fused, q_rot)
     assert torch.equal(kc2.view(torch.uint8), kc.view(torch.uint8))
     assert torch.equal(vc2.view(torch.uint8), vc.view(torch.uint8))
+
+
+def _strided_copy(x):
+    """Same values with inner stride 2: the scalar append/RoPE kernels take it."""
+    wide = torch.empty(*x.shape[:-1], 2 * x.shape[-1], dtype=x.dtype, device=x.device)
+    view = wide[..., ::2]
+    view.copy_(x)
+    return view
+
+
+@pytest.mark.parametrize("cache", ["same", "fp8"])
+@pytest.mark.parametrize("interleaved", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_vectorized_append_and_rope_match_scalar_kernels(device, cache, interleaved, dtype):
+    from flash_attn_b200._cache import append_kvcache, rotary_append_kvcache
+    cache_dtype = dtype if cache == "same" else torch.float8_e4m3fn
+    g = torch.Generator().manual_seed(62)
+    B, S, H, HK, D, page = 4, 300, 16, 8, 128, 16
+    cols = (S + 40) // page + 1
+    q = torch.randn(B, S, H, D, generator=g).to(dtype).to(device)
+    k = (torch.randn(B, S, HK, D, generator=g) * 3).to(dtype).to(device)
+    v = (torch.randn(B, S, HK, D, generator=g) * 3).to(dtype).to(device)
+    angles = torch.rand(cols * page, D // 2, generator=g) * 6
+    cos, sin = angles.cos().to(device), angles.sin().to(device)
+    table = torch.randperm(B * cols, generator=g).int().reshape(B, cols).to(device)
+    lengths = torch.tensor([0, 3, 40, 17], dtype=torch.int32, device=device)
+    scale = torch.tensor([.01 * (i + 1) for i in range(HK)], device=device) \
+        if cache_dtype == torch.float8_e4m3fn else None
+    caches = [torch.zeros(B * cols, page, HK, D, dtype=cache_dtype, device=device) for _ in range(8)]
+    # Plain append: vectorized (contiguous) vs scalar (strided inputs).
+    append_kvcache(k, v, caches[0], caches[1], lengths, block_table=table, k_scale=scale, v_scale=scale)
+    append_kvcache(_strided_copy(k), _strided_copy(v), caches[2], caches[3], lengths, block_table=table,
+                   k_scale=scale, v_scale=scale)
+    assert torch.equal(caches[0].view(torch.uint8), caches[2].view(torch.uint8))
+    assert torch.equal(caches[1].view(torch.uint8), caches[3].view(torch.uint8))
+    # Fused RoPE + append.
+    kw = dict(rotary_interleaved=interleaved, causal=True, block_table=table, k_scale=scale, v_scale=scale)
+    q_vec = rotary_append_kvcache(q, k, v, caches[4], caches[5], cos, sin, lengths, **kw)
+    q_sca = rotary_append_kvcache(_strided_copy(q), _strided_copy(k), _strided_copy(v), caches[6], caches[7],
+                                  cos, sin, lengths, **kw)
+    assert torch.equal(q_vec, q_sca)
+    assert torch.equal(caches[4].view(torch.uint8), caches[6].view(torch.uint8))
+    assert torch.equal(caches[5].view(torch.uint8), caches[7].view(torch.uint8))
+    assert caches[4].view(torch.uint8).any()

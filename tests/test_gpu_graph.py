@@ -109,3 +109,19 @@ def test_varlen_prefill_replays(device):
         expected, expected_lse = step()
         torch.cuda.synchronize()
         assert torch.equal(out, expected) and torch.equal(lse, expected_lse), trial
+
+
+def test_launch_counter_counts_captures_not_replays(device):
+    from flash_attn_b200 import _capi
+    k = torch.randn(32, 2, 128, device=device).to(torch.bfloat16)
+    cache = torch.zeros(4, 16, 2, 128, dtype=torch.bfloat16, device=device)
+    slots = torch.arange(32, device=device)
+    before = _capi.kernel_launches()
+    store_kvcache(k, k, cache, cache.clone(), slots)
+    assert _capi.kernel_launches() - before == 1
+    graph, _ = _capture(lambda: store_kvcache(k, k, cache, cache.clone(), slots))
+    captured = _capi.kernel_launches()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert _capi.kernel_launches() == captured
