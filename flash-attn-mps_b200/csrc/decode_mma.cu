@@ -543,7 +543,11 @@ int page_shift_of(const AttnParams& p) {
 // CTA shape: consumer warps per CTA (16 tokens each per stage), pipeline
 // stages and the occupancy bound, per K/V storage type. Measured on B200 with
 // the TMA gather: FP8 4 warps x 3 stages x 4 CTAs/SM (48 KB ring each) beat
-// 8 x 3 x 2 by 2-3% on 64 x 131072-token contexts; bf16 keeps 4 x 3 x 2.
+// 8 x 3 x 2 by 2-3% on 64 x 131072-token contexts. 16-bit K/V: 2 warps x 3
+// stages x 4 CTAs/SM (48 KB ring) beat 4 x 3 x 2 (96 KB) by 17% at 64 x 1152
+// tokens, 7% at 64 x 4096 and 1% on config 3 (256 x U[512, 32768]): with more,
+// smaller CTAs per SM one CTA's prologue and pipeline fill overlap the others'
+// streaming; 4 x 2 x 3, 2 x 2 x 5, 2 x 4 x 3 and 1 x 4 x 8 measured slower.
 #ifndef FAB_DECODE_FP8_W
 #define FAB_DECODE_FP8_W 4
 #endif
@@ -554,16 +558,19 @@ int page_shift_of(const AttnParams& p) {
 #define FAB_DECODE_FP8_MINB 4
 #endif
 #ifndef FAB_DECODE_16_W
-#define FAB_DECODE_16_W 4
+#define FAB_DECODE_16_W 2
 #endif
 #ifndef FAB_DECODE_16_NST
 #define FAB_DECODE_16_NST 3
 #endif
 #ifndef FAB_DECODE_16_MINB
-#define FAB_DECODE_16_MINB 2
+#define FAB_DECODE_16_MINB 4
 #endif
-#ifndef FAB_DECODE_MIN_SPLITS
-#define FAB_DECODE_MIN_SPLITS 4
+#ifndef FAB_DECODE_FP8_MIN_SPLITS
+#define FAB_DECODE_FP8_MIN_SPLITS 4
+#endif
+#ifndef FAB_DECODE_16_MIN_SPLITS
+#define FAB_DECODE_16_MIN_SPLITS 4
 #endif
 #ifndef FAB_DECODE_TMA
 #define FAB_DECODE_TMA 1
@@ -673,11 +680,22 @@ int decode_default_splits(const AttnParams& p, int* span) {
   const int group = p.HQ / p.HK;
   const int64_t units = (int64_t)p.B * p.HK * ((group + 15) / 16);
   const int by_len = max(1, (eff + 255) / 256);
-  const int want = (int)((8LL * sm_count() + units - 1) / units);
-  // Few long splits amortise each CTA's prologue and pipeline fill (measured:
-  // 4 splits beat 8..32 on both uniform 131072-token and ragged 512..32768
-  // contexts); more splits only when the grid would not fill the SMs.
-  int splits = max(want, FAB_DECODE_MIN_SPLITS);
+  int splits;
+  if (p.kt == FA_E4M3) {
+    // Few long splits amortise each CTA's prologue and pipeline fill (measured:
+    // 4 splits beat 8..32 on uniform 131072-token contexts); more splits only
+    // when the grid would not fill the SMs.
+    const int want = (int)((8LL * sm_count() + units - 1) / units);
+    splits = max(want, FAB_DECODE_FP8_MIN_SPLITS);
+  } else {
+    // When one split per (request, KV head) already fills the resident CTA
+    // slots, 4 splits keep a ragged batch from ending on its longest request
+    // (config 3: 6.83 TB/s vs 6.22 with 1); otherwise about 1.7 CTAs per slot
+    // (64 x 1152..16384 tokens: 2 splits beat 3 and 4 by 3-13%).
+    const int64_t slots = (int64_t)sm_count() * FAB_DECODE_16_MINB;
+    const int want = (int)((17 * slots + 10 * units - 1) / (10 * units));
+    splits = max(want, units >= slots ? FAB_DECODE_16_MIN_SPLITS : 2);
+  }
   splits = max(1, min(splits, by_len));
   *span = (eff + splits - 1) / splits;
   return splits;
