@@ -460,6 +460,7 @@ struct VecSide {
   int64_t ds0, ds1, ds2;           // cache [N|rows, P|cap, H, D], or q_out [B,S,H,D]
   const float* scale; int64_t scale_stride;
   int32_t H, V, fp8, rotate;       // V = D / 8
+  int32_t vshift;                  // log2(V), or -1 when V is not a power of two
 };
 
 struct VecArgs {
@@ -470,6 +471,7 @@ struct VecArgs {
   const int32_t* batch_idx; int64_t bi_stride;
   const int32_t* table; int64_t bt0, bt1;
   int32_t paged, pages_per_seq, P, remap, S;
+  int32_t pshift;                  // log2(P), or -1 when P is not a power of two
   int64_t blocks, rows, tokens;
 };
 
@@ -523,93 +525,99 @@ __device__ __forceinline__ void put8(const VecSide& s, uint8_t* row, int e, cons
 }
 
 template <typename T>
-__global__ void __launch_bounds__(256) rope_append_vec_kernel(VecArgs a) {
+__global__ void __launch_bounds__(128) rope_append_vec_kernel(VecArgs a) {
   const int which = blockIdx.y;
   const VecSide& s = a.side[which];
   if (s.x == nullptr) return;
   const int units = s.H * s.V;
-  const int64_t total = a.tokens * units;
-  const int64_t step = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += step) {
-    int64_t tok;
-    int u;
-    if (total <= 0x7fffffff) {
-      const uint32_t ee = (uint32_t)e;
-      tok = ee / (uint32_t)units;
-      u = (int)(ee - (uint32_t)tok * (uint32_t)units);
-    } else {
-      tok = e / units;
-      u = (int)(e - tok * units);
-    }
-    const int h = u / s.V;
-    const int c0 = (u - h * s.V) * 8;
-    const int64_t b = tok / a.S;
+  const int64_t dst_elt = which != 2 && s.fp8 ? 1 : (int64_t)sizeof(T);
+  // One token row (all heads) per block iteration: the row geometry (request,
+  // position, page) is computed once per token, heads and vectors by shifts.
+  for (int64_t tok = blockIdx.x; tok < a.tokens; tok += gridDim.x) {
+    const int64_t b = tok <= 0x7fffffff ? (int64_t)((uint32_t)tok / (uint32_t)a.S) : tok / a.S;
     const int j = (int)(tok - b * a.S);
     const int64_t len = a.lengths[b * a.len_stride];
     int64_t pos;
-    uint8_t* out;
+    uint8_t* out_tok;
     if (which == 2) {
       pos = len + (a.advance_q ? j : 0);
-      out = s.dst + (b * s.ds0 + j * s.ds1 + h * s.ds2) * (int64_t)sizeof(T);
+      out_tok = s.dst + (b * s.ds0 + j * s.ds1) * dst_elt;
     } else {
       pos = len + j;
       const int64_t row = a.remap ? (int64_t)a.batch_idx[b * a.bi_stride] : b;
       const int64_t capacity = a.paged ? (int64_t)a.pages_per_seq * a.P : a.P;
       if (row < 0 || row >= a.rows || pos < 0 || pos >= capacity) continue;
-      const int64_t block = a.paged ? (int64_t)a.table[row * a.bt0 + (pos / a.P) * a.bt1] : row;
+      int64_t block = row, offset = pos;
+      if (a.paged) {
+        const int64_t pg = a.pshift >= 0 ? (pos >> a.pshift) : pos / a.P;
+        block = a.table[row * a.bt0 + pg * a.bt1];
+        offset = pos - pg * a.P;
+      }
       if (block < 0 || block >= a.blocks) continue;
-      const int64_t offset = a.paged ? pos % a.P : pos;
-      out = s.dst + (block * s.ds0 + offset * s.ds1 + h * s.ds2) * (int64_t)(s.fp8 ? 1 : sizeof(T));
+      out_tok = s.dst + (block * s.ds0 + offset * s.ds1) * dst_elt;
     }
-    const uint8_t* in = s.x + (b * s.xs0 + j * s.xs1 + h * s.xs2) * (int64_t)sizeof(T);
-    const float scale = s.fp8 && s.scale ? s.scale[h * s.scale_stride] : 1.0f;
-    const bool rotated = s.rotate && c0 < 2 * a.half;
-    if (!rotated) {
-      if (!s.fp8) {
-        *reinterpret_cast<uint4*>(out + (int64_t)c0 * sizeof(T)) =
-            __ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T)));
+    const uint8_t* in_tok = s.x + (b * s.xs0 + j * s.xs1) * (int64_t)sizeof(T);
+    for (int u = threadIdx.x; u < units; u += blockDim.x) {
+      const int h = s.vshift >= 0 ? (u >> s.vshift) : u / s.V;
+      const int c0 = (u - h * s.V) * 8;
+      uint8_t* out = out_tok + h * s.ds2 * dst_elt;
+      const uint8_t* in = in_tok + h * s.xs2 * (int64_t)sizeof(T);
+      const float scale = s.fp8 && s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+      const bool rotated = s.rotate && c0 < 2 * a.half;
+      if (!rotated) {
+        if (!s.fp8) {
+          *reinterpret_cast<uint4*>(out + (int64_t)c0 * sizeof(T)) =
+              __ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T)));
+        } else {
+          float f[8];
+          unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), f);
+          put8<T>(s, out, c0, f, scale);
+        }
+        continue;
+      }
+      if (a.interleaved) {
+        // Pairs (c0 + 2k, c0 + 2k + 1) use angle index c0/2 + k.
+        float x[8], o[8];
+        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x);
+        const float4 cv = __ldg(reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0 / 2));
+        const float4 sv = __ldg(reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0 / 2));
+        const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          o[2 * k] = __fadd_rn(__fmul_rn(x[2 * k], cc[k]), -__fmul_rn(x[2 * k + 1], ss[k]));
+          o[2 * k + 1] = __fadd_rn(__fmul_rn(x[2 * k + 1], cc[k]), __fmul_rn(x[2 * k], ss[k]));
+        }
+        put8<T>(s, out, c0, o, scale);
       } else {
-        float f[8];
-        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), f);
-        put8<T>(s, out, c0, f, scale);
-      }
-      continue;
-    }
-    if (a.interleaved) {
-      // Pairs (c0 + 2k, c0 + 2k + 1) use angle index c0/2 + k.
-      float x[8], o[8];
-      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x);
-      const float4 cv = __ldg(reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0 / 2));
-      const float4 sv = __ldg(reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0 / 2));
-      const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+        if (c0 >= a.half) continue;  // the partner vector at c0 - half writes this one
+        float x1[8], x2[8], o1[8], o2[8];
+        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x1);
+        unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)(c0 + a.half) * sizeof(T))), x2);
+        const float4* cp = reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0);
+        const float4* sp = reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0);
+        const float4 ca = __ldg(cp), cb = __ldg(cp + 1), sa = __ldg(sp), sb = __ldg(sp + 1);
+        const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+        const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        o[2 * k] = __fadd_rn(__fmul_rn(x[2 * k], cc[k]), -__fmul_rn(x[2 * k + 1], ss[k]));
-        o[2 * k + 1] = __fadd_rn(__fmul_rn(x[2 * k + 1], cc[k]), __fmul_rn(x[2 * k], ss[k]));
+        for (int k = 0; k < 8; ++k) {
+          o1[k] = __fadd_rn(__fmul_rn(x1[k], cc[k]), -__fmul_rn(x2[k], ss[k]));
+          o2[k] = __fadd_rn(__fmul_rn(x2[k], cc[k]), __fmul_rn(x1[k], ss[k]));
+        }
+        put8<T>(s, out, c0, o1, scale);
+        put8<T>(s, out, c0 + a.half, o2, scale);
       }
-      put8<T>(s, out, c0, o, scale);
-    } else {
-      if (c0 >= a.half) continue;  // the partner vector at c0 - half writes this one
-      float x1[8], x2[8], o1[8], o2[8];
-      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T))), x1);
-      unpack8<T>(__ldg(reinterpret_cast<const uint4*>(in + (int64_t)(c0 + a.half) * sizeof(T))), x2);
-      const float4* cp = reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0);
-      const float4* sp = reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0);
-      const float4 ca = __ldg(cp), cb = __ldg(cp + 1), sa = __ldg(sp), sb = __ldg(sp + 1);
-      const float cc[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-      const float ss[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        o1[k] = __fadd_rn(__fmul_rn(x1[k], cc[k]), -__fmul_rn(x2[k], ss[k]));
-        o2[k] = __fadd_rn(__fmul_rn(x2[k], cc[k]), __fmul_rn(x1[k], ss[k]));
-      }
-      put8<T>(s, out, c0, o1, scale);
-      put8<T>(s, out, c0 + a.half, o2, scale);
     }
   }
 }
 
 inline bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
+
+inline int log2_exact(int64_t v) {
+  if (v <= 0 || (v & (v - 1))) return -1;
+  int k = 0;
+  while ((int64_t(1) << k) < v) ++k;
+  return k;
+}
 
 // Launch the vectorized kernel when every operand qualifies; returns 1 when it
 // did not apply (the caller runs the scalar kernel), else FA_OK / an error.
@@ -663,16 +671,18 @@ int launch_rope_append_vec(const AppendArgs& a, const RopeArgs* r, int64_t batch
   v.table = a.table; v.bt0 = a.bt0; v.bt1 = a.bt1;
   v.paged = a.paged; v.pages_per_seq = a.pages_per_seq; v.P = a.P; v.remap = a.remap;
   v.blocks = a.blocks; v.rows = a.rows; v.tokens = batch * v.S;
-  int64_t vectors = 0;
+  v.pshift = log2_exact(a.P);
+  bool work = false;
   for (int i = 0; i < 3; ++i)
     if (v.side[i].x) {
-      const int64_t n = v.tokens * v.side[i].H * v.side[i].V;
-      vectors = n > vectors ? n : vectors;
+      v.side[i].vshift = log2_exact(v.side[i].V);
+      work = work || (int64_t)v.side[i].H * v.side[i].V > 0;
     }
-  if (vectors == 0) return FA_OK;
-  const dim3 grid(grid_for(vectors), sides);
-  if (dtype == FA_BF16) rope_append_vec_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(v);
-  else rope_append_vec_kernel<__half><<<grid, 256, 0, stream>>>(v);
+  if (v.tokens == 0 || !work) return FA_OK;
+  const int64_t cap = (int64_t)sm_count() * 16;
+  const dim3 grid((unsigned)(v.tokens < cap ? v.tokens : cap), sides);
+  if (dtype == FA_BF16) rope_append_vec_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(v);
+  else rope_append_vec_kernel<__half><<<grid, 128, 0, stream>>>(v);
   note_launch();
   FAB_LAUNCH_CHECK("vectorized append launch");
   return FA_OK;
