@@ -43,14 +43,30 @@ namespace {
 using namespace sm100;
 
 constexpr int BM = 128;          // query rows per tile (two tiles per CTA)
-constexpr int BN = 128;          // keys per tile
-constexpr int HD = 128;          // largest head dim (shared-memory slots are sized for it)
-#ifndef FAB_PREFILL_NSLOT
-#define FAB_PREFILL_NSLOT 3
+#ifndef FAB_PREFILL_BN
+#define FAB_PREFILL_BN 128
 #endif
-constexpr int NSLOT = FAB_PREFILL_NSLOT;  // K/V ring slots (each holds one K or one V tile)
-constexpr int kRegion = 128 * 128;            // one 128-row x 64-element box (bytes)
-constexpr int kTileBytes = 2 * kRegion;       // 128 x 128 bf16
+constexpr int BN = FAB_PREFILL_BN;  // keys per tile
+static_assert(BN == 64 || BN == 128, "key tile");
+// S/P buffers per query tile: its 128 TMEM columns hold SBUF score tiles of BN
+// columns, so with BN = 64 QK^T of key tile j+2 runs while the softmax works
+// on j. Measured on B200 (clock64 traces, non-causal 4096 keys): each M=128
+// K=16 tcgen05.mma step costs ~90 cycles at N=64 as at N=128, so the 64-key
+// schedule's 24 smaller MMAs per 64 keys take ~3950 cycles -- slower than the
+// 128-key chain (1160 -> 648 TFLOP/s non-causal, 888 -> 562 on config 2).
+// BN = 128 (one S buffer) is the default; BN = 64 stays correct and selectable.
+constexpr int SBUF = 128 / BN;
+#ifndef FAB_PREFILL_NSLOT
+#define FAB_PREFILL_NSLOT 0
+#endif
+// K/V ring slots (each holds one K or one V tile), 96 KB in all. With SBUF = 2
+// the MMA warp needs K(j+2) before it releases V(j): at least 4 slots.
+constexpr int NSLOT = FAB_PREFILL_NSLOT > 0 ? FAB_PREFILL_NSLOT : 3 * SBUF;
+static_assert(SBUF == 1 || NSLOT >= 4, "ring too shallow for the QK look-ahead");
+constexpr int kRegion = 128 * 128;            // one 128-row x 64-element Q box (bytes)
+constexpr int kTileBytes = 2 * kRegion;       // 128 x 128 bf16 Q tile
+constexpr int kKVRegion = BN * 128;           // one BN-row x 64-element K/V box
+constexpr int kKVTileBytes = 2 * kKVRegion;   // BN x 128 bf16 K or V tile
 constexpr int kThreads = 384;                 // 2 softmax warpgroups + (TMA, MMA, 2 idle) warpgroup
 // Registers: the CTA launches with kLaunchRegs per thread (checked on the host
 // before every launch); the producer warpgroup gives registers back and the
@@ -70,13 +86,13 @@ static_assert(kLaunchRegs * kThreads <= 65536, "launch registers");
 constexpr int OFF_QA = 0;
 constexpr int OFF_QB = OFF_QA + kTileBytes;
 constexpr int OFF_RING = OFF_QB + kTileBytes;
-constexpr int OFF_STAGE = OFF_RING + NSLOT * kTileBytes;  // 8 softmax warps x [2][32 rows][128 B]
+constexpr int OFF_STAGE = OFF_RING + NSLOT * kKVTileBytes;  // 8 softmax warps x [2][32 rows][128 B]
 constexpr int kStageWarpBytes = 2 * 32 * 128;
 constexpr int OFF_BAR = OFF_STAGE + 8 * kStageWarpBytes;
 // Barriers, TMEM holder, work-id ring and item ring, then alignment slack.
 constexpr int kSmemBytes = OFF_BAR + 1024 + 1024;
 constexpr int NWORK = 4;  // work-id ring slots
-constexpr uint32_t kTmemCols = 512;           // S_A, S_B, O_A, O_B (128 fp32 columns each)
+constexpr uint32_t kTmemCols = 512;           // S_A, S_B, O_A, O_B (128 fp32 columns each; S as SBUF tiles)
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays <= 2^8 between rescales
 #ifndef FAB_PREFILL_POLY_PAIRS
@@ -88,9 +104,12 @@ constexpr float kRescaleThreshold = 8.0f;     // log2 units: P stays <= 2^8 betw
 // MUFU-bound), so the default keeps every exponential on MUFU.
 constexpr int kPolyPairs = FAB_PREFILL_POLY_PAIRS;
 
+// Per query tile t (0 = A, 1 = B) and S buffer b: B_SF + t*SBUF + b (scores
+// ready), B_PF + t*SBUF + b (P ready, 128 arrivals); B_PVD + t (a PV finished).
 enum {
-  B_Q = 0, B_QE, B_FULL, B_EMPTY = B_FULL + NSLOT, B_SFA = B_EMPTY + NSLOT, B_SFB, B_PFA, B_PFB, B_ODA, B_ODB,
-  B_FIN, B_WFULL, B_WEMPTY = B_WFULL + NWORK, B_COUNT = B_WEMPTY + NWORK
+  B_Q = 0, B_QE, B_FULL, B_EMPTY = B_FULL + NSLOT, B_SF = B_EMPTY + NSLOT, B_PF = B_SF + 2 * SBUF,
+  B_PVD = B_PF + 2 * SBUF, B_ODA = B_PVD + 2, B_ODB, B_FIN, B_WFULL, B_WEMPTY = B_WFULL + NWORK,
+  B_COUNT = B_WEMPTY + NWORK
 };
 
 __device__ int g_prefill_timeout;
@@ -348,7 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                          const PrefillParams p) {
   static_assert(HDIM == 64 || HDIM == 128, "head dim");
   constexpr int kHalves = HDIM / 64;             // 64-element regions per row
-  constexpr int kLoadBytes = kHalves * kRegion;  // bytes of one Q/K/V tile actually loaded
+  constexpr int kLoadBytes = kHalves * kRegion;      // bytes of one Q tile actually loaded
+  constexpr int kKVLoadBytes = kHalves * kKVRegion;  // bytes of one K/V tile actually loaded
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_addr(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -381,10 +401,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_FULL + s), 1);
       mbar_init(bar(B_EMPTY + s), 1);
     }
-    mbar_init(bar(B_SFA), 1);
-    mbar_init(bar(B_SFB), 1);
-    mbar_init(bar(B_PFA), 128);
-    mbar_init(bar(B_PFB), 128);
+    for (int b = 0; b < 2 * SBUF; ++b) {
+      mbar_init(bar(B_SF + b), 1);
+      mbar_init(bar(B_PF + b), 128);
+    }
+    mbar_init(bar(B_PVD), 1);
+    mbar_init(bar(B_PVD + 1), 1);
     mbar_init(bar(B_ODA), 1);
     mbar_init(bar(B_ODB), 1);
     mbar_init(bar(B_FIN), 1);
@@ -451,23 +473,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t slot = items % NSLOT;
         if (items >= NSLOT && !(ok = warp_wait(bar(B_EMPTY + slot), ((items / NSLOT) - 1) & 1))) break;
         const CUtensorMap* map = (i & 1) ? &tv : &tk;
-        const uint32_t dst = base + OFF_RING + slot * kTileBytes;
+        const uint32_t dst = base + OFF_RING + slot * kKVTileBytes;
         if (p.table == nullptr) {
           if (lane == 0) {
             const int row = it.k_begin + (it.j_first + (i >> 1)) * BN;
-            mbar_expect_tx(bar(B_FULL + slot), kLoadBytes);
+            mbar_expect_tx(bar(B_FULL + slot), kKVLoadBytes);
 #pragma unroll
             for (int hf = 0; hf < kHalves; ++hf)
-              tma_load_3d(dst + hf * kRegion, map, bar(B_FULL + slot), hf * 64, it.kh, row);
+              tma_load_3d(dst + hf * kKVRegion, map, bar(B_FULL + slot), hf * 64, it.kh, row);
           }
         } else {
-          // Paged K/V: the tile's 128 keys arrive as page boxes (box_rows
+          // Paged K/V: the tile's BN keys arrive as page boxes (box_rows
           // tokens x 64 head dims each, one lane per box) through
           // block_table; pages past the sequence or the table use page -1,
           // which TMA fills with zeros.
           const int nb = BN / p.box_rows;
           const int key0 = (it.j_first + (i >> 1)) * BN;
-          if (lane == 0) mbar_expect_tx(bar(B_FULL + slot), kLoadBytes);
+          if (lane == 0) mbar_expect_tx(bar(B_FULL + slot), kKVLoadBytes);
           __syncwarp();
           if (lane < kHalves * nb) {
             const int half = lane / nb, c = lane - half * nb;
@@ -475,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pg = pos >> p.page_shift;
             int blk = -1;
             if (pos < it.k_len && pg < p.bt_cols) blk = __ldg(p.table + (int64_t)it.b * p.bt0 + (int64_t)pg * p.bt1);
-            tma_load_4d(dst + half * kRegion + c * p.box_rows * 128, map, bar(B_FULL + slot), half * 64, it.kh,
+            tma_load_4d(dst + half * kKVRegion + c * p.box_rows * 128, map, bar(B_FULL + slot), half * 64, it.kh,
                         pos & ((1 << p.page_shift) - 1), blk);
           }
           __syncwarp();
@@ -491,27 +513,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- MMA
     const uint32_t idesc_qk = f16_idesc(BM, BN, BF16 ? 1 : 0, 0);
     const uint32_t idesc_pv = f16_idesc(BM, HDIM, BF16 ? 1 : 0, 1);
-    const uint32_t tSA = tmem, tSB = tmem + 128, tOA = tmem + 256, tOB = tmem + 384;
-    auto slot_addr = [&](uint32_t item) { return base + OFF_RING + (item % NSLOT) * kTileBytes; };
+    auto slot_addr = [&](uint32_t item) { return base + OFF_RING + (item % NSLOT) * kKVTileBytes; };
     auto wait_item = [&](uint32_t item) { return warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1); };
+    // S tile number n of query tile t lives in TMEM columns t*128 + (n % SBUF)*BN.
+    auto s_tmem = [&](int t, uint32_t n) { return tmem + (uint32_t)(t * 128) + (n % SBUF) * (uint32_t)BN; };
     auto qk = [&](uint32_t q_off, uint32_t kaddr, uint32_t d, int sfbar) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < HDIM / 16; ++kk) {
           const uint64_t a = sw128_desc(base + q_off + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kRegion + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(kaddr + (kk >> 2) * kKVRegion + (kk & 3) * 32, 16, 1024);
           mma_f16_ss(d, a, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
         mma_commit(bar(sfbar));
       }
       __syncwarp();
     };
-    // P (M=128 rows x K=128 keys) is the A operand in TMEM: 16 keys = 8 columns.
+    // P (M=128 rows x K=BN keys) is the A operand in TMEM: 16 keys = 8 columns.
     auto pv = [&](uint32_t p_tmem, uint32_t vaddr, uint32_t d, bool acc) {
       if (lane == 0) {
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t bd = sw128_desc(vaddr + kk * 2048, kRegion, 1024);
+          const uint64_t bd = sw128_desc(vaddr + kk * 2048, kKVRegion, 1024);
           mma_f16_ts(d, p_tmem + kk * 8, bd, idesc_pv, (acc || kk > 0) ? 1u : 0u);
         }
       }
@@ -521,8 +544,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mma_commit(bar(barid));
       __syncwarp();
     };
-    uint32_t items = 0, qloads = 0, pa = 0, pb = 0, wcnt = 0;
+    // Per query tile t: nq[t] QK^T and np[t] PV issued so far (S buffer and
+    // barrier phase of each follow from these counts on both sides).
+    uint32_t items = 0, qloads = 0, wcnt = 0;
+    uint32_t nqa = 0, nqb = 0, npa = 0, npb = 0;
     bool ok = true;
+    auto issue_qk = [&](int t, uint32_t& nq, uint32_t kaddr) {
+      qk(t ? OFF_QB : OFF_QA, kaddr, s_tmem(t, nq), B_SF + t * SBUF + (int)(nq % SBUF));
+      ++nq;
+    };
+    // PV of query tile t once its softmax has published P; false on timeout.
+    auto issue_pv = [&](int t, uint32_t& np, uint32_t vaddr, bool acc) {
+      const uint32_t n = np;
+      if (!warp_wait(bar(B_PF + t * SBUF + (int)(n % SBUF)), (n / SBUF) & 1)) return false;
+      tc_fence_after();
+      pv(s_tmem(t, n), vaddr, tmem + 256 + (uint32_t)(t * 128), acc);
+      ++np;
+      if constexpr (SBUF > 1) commit(B_PVD + t);
+      return true;
+    };
     while (ok) {
       Item it;
       const int w = next_work(wcnt, it);
@@ -530,39 +570,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (it.n_all == 0) continue;
       auto act_a = [&](int j) { return j >= it.a0 && j < it.a1; };
       auto act_b = [&](int j) { return j >= it.b0 && j < it.b1; };
-      if (!(ok = warp_wait(bar(B_Q), qloads & 1) && wait_item(items))) break;
+      if (!(ok = warp_wait(bar(B_Q), qloads & 1))) break;
       ++qloads;
-      tc_fence_after();
-      if (act_a(it.j_first)) qk(OFF_QA, slot_addr(items), tSA, B_SFA);
-      if (act_b(it.j_first)) qk(OFF_QB, slot_addr(items), tSB, B_SFB);
-      commit(B_EMPTY + items % NSLOT);
-      if (it.n_all == 1) commit(B_QE);
+      // QK^T of the first SBUF key tiles, then per tile j: PV(j) of A, QK^T(j+SBUF)
+      // of A, PV(j) of B, QK^T(j+SBUF) of B, so a tile's scores for j+1..j+SBUF
+      // are computed while its softmax works on j.
+      const int pre = it.n_all < SBUF ? it.n_all : SBUF;
+      for (int t = 0; t < pre; ++t) {
+        const uint32_t ik = items + 2 * t;
+        if (!(ok = wait_item(ik))) break;
+        tc_fence_after();
+        if (act_a(it.j_first + t)) issue_qk(0, nqa, slot_addr(ik));
+        if (act_b(it.j_first + t)) issue_qk(1, nqb, slot_addr(ik));
+        commit(B_EMPTY + ik % NSLOT);
+      }
+      if (!ok) break;
+      if (it.n_all <= SBUF) commit(B_QE);
       for (int t = 0; ok && t < it.n_all; ++t) {
         const int j = it.j_first + t;
-        const uint32_t iv = items + 2 * t + 1, ik = items + 2 * t + 2;
+        const uint32_t iv = items + 2 * t + 1, ik = items + 2 * (t + SBUF);
+        const bool next = t + SBUF < it.n_all;
         if (!(ok = wait_item(iv))) break;
         if (act_a(j)) {
-          if (!(ok = warp_wait(bar(B_PFA), pa & 1))) break;
-          ++pa;
-          tc_fence_after();
-          pv(tSA, slot_addr(iv), tOA, j > it.a0);
+          if (!(ok = issue_pv(0, npa, slot_addr(iv), j > it.a0))) break;
           if (j == it.a1 - 1) commit(B_ODA);
         }
-        const bool next = t + 1 < it.n_all;
         if (next && !(ok = wait_item(ik))) break;
         tc_fence_after();
-        if (next && act_a(j + 1)) qk(OFF_QA, slot_addr(ik), tSA, B_SFA);
+        if (next && act_a(j + SBUF)) issue_qk(0, nqa, slot_addr(ik));
         if (act_b(j)) {
-          if (!(ok = warp_wait(bar(B_PFB), pb & 1))) break;
-          ++pb;
-          tc_fence_after();
-          pv(tSB, slot_addr(iv), tOB, j > it.b0);
+          if (!(ok = issue_pv(1, npb, slot_addr(iv), j > it.b0))) break;
           if (j == it.b1 - 1) commit(B_ODB);
         }
         commit(B_EMPTY + iv % NSLOT);
-        if (next && act_b(j + 1)) qk(OFF_QB, slot_addr(ik), tSB, B_SFB);
+        if (next && act_b(j + SBUF)) issue_qk(1, nqb, slot_addr(ik));
         if (next) commit(B_EMPTY + ik % NSLOT);
-        if (t + 2 == it.n_all) commit(B_QE);  // the item's last QK^T has been issued
+        if (t + SBUF + 1 == it.n_all) commit(B_QE);  // the item's last QK^T has been issued
       }
       items += 2 * it.n_all;
     }
@@ -577,9 +620,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = (uint32_t)(sub * 32) << 16;
-    const uint32_t tS = tmem + (is_b ? 128 : 0) + lane_off;
+    const int tq = is_b ? 1 : 0;
+    const uint32_t tS0 = tmem + (uint32_t)(tq * 128) + lane_off;
     const uint32_t tO = tmem + (is_b ? 384 : 256) + lane_off;
-    const int sf = is_b ? B_SFB : B_SFA, pf = is_b ? B_PFB : B_PFA, od = is_b ? B_ODB : B_ODA;
+    const int od = is_b ? B_ODB : B_ODA;
+    // s_cnt: score tiles consumed (= P tiles published) by this warpgroup; tile
+    // n uses S buffer n % SBUF and phase n / SBUF of that buffer's barriers.
     uint32_t s_cnt = 0, o_cnt = 0, items = 0, wcnt = 0;
     bool ok = true;
     while (ok) {
@@ -599,22 +645,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_run = it.sink_l2, l_run = p.sinks ? 1.f : 0.f;
       for (int jj = 0; jj < n_x; ++jj) {
         const int j = x0 + jj;
-        if (!(ok = warp_wait(bar(sf), s_cnt & 1))) break;
+        const int sbuf = (int)(s_cnt % SBUF);
+        if (!(ok = warp_wait(bar(B_SF + tq * SBUF + sbuf), (s_cnt / SBUF) & 1))) break;
         ++s_cnt;
         tc_fence_after();
+        const uint32_t tS = tS0 + (uint32_t)(sbuf * BN);
         const int key0 = j * BN;
         const int c_lo = vis.lo - key0, c_hi = vis.hi - key0;  // visible columns of this tile
         const bool need_mask = c_lo > 0 || c_hi < BN - 1;
-        // The whole S row in registers: four TMEM loads, one wait.
-        uint32_t r[128];
+        // The whole S row of the tile in registers: BN/32 TMEM loads, one wait.
+        uint32_t r[BN];
         tmem_ld32_at<0>(tS, r);
         tmem_ld32_at<32>(tS + 32, r);
-        tmem_ld32_at<64>(tS + 64, r);
-        tmem_ld32_at<96>(tS + 96, r);
+        if constexpr (BN == 128) {
+          tmem_ld32_at<64>(tS + 64, r);
+          tmem_ld32_at<96>(tS + 96, r);
+        }
         tmem_wait_ld();
         if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
+          for (int i = 0; i < BN; ++i)
             if (i < c_lo || i > c_hi) r[i] = __float_as_uint(-INFINITY);
         }
         // Row max as 8 independent 3-input max chains (exact in any order).
@@ -622,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k8 = 0; k8 < 8; ++k8) mx8[k8] = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 128; i += 2)
+        for (int i = 0; i < BN; i += 2)
           mx8[(i >> 1) & 7] = max3(mx8[(i >> 1) & 7], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
@@ -636,8 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         l_run *= factor;
         const float msub = m_run == -INFINITY ? 0.f : m_run;
         // P = 2^(s*scale_log2 - m), masked columns -> 0, packed as 16-bit pairs
-        // into TMEM columns [0, 64) of this row's S, 8 columns per store; the
-        // row sum runs as 8 independent chains (4 packed pairs).
+        // into TMEM columns [0, BN/2) of this row's S tile, 8 columns per store;
+        // the row sum runs as 8 independent chains (4 packed pairs).
         uint64_t ls2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
@@ -648,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
         const Exp2Poly<BF16> poly;  // degree 3 for bf16 P, 4 for f16 P
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int c8 = 0; c8 < BN / 16; ++c8) {
           uint32_t pk[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -686,9 +736,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st8_at<0>(tS + c8 * 8, pk);
         }
         // Lazy O rescale (after the exponentials, while S no longer occupies
-        // registers); PV(j) is issued only after this row's P-ready arrival,
-        // and PV(j-1) completed before S(j) was signalled.
+        // registers). PV(j) is issued only after this row's P-ready arrival.
+        // With one S buffer, PV(j-1) completed before S(j) was signalled; with
+        // SBUF buffers S(j) only follows PV(j-SBUF), so wait for PV(j-1) (the
+        // s_cnt-1'th PV of this tile, at most one phase behind) first.
         if (jj > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+          if constexpr (SBUF > 1) {
+            if (!(ok = warp_wait(bar(B_PVD + tq), (s_cnt - 2) & 1))) break;
+            tc_fence_after();
+          }
 #pragma unroll
           for (int c = 0; c < HDIM / 32; ++c) {
             uint32_t o[32];
@@ -711,19 +767,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           // warpgroup consuming the tile zeroes them itself (identical stores).
           const uint32_t item = items + 2 * (j - it.j_first) + 1;
           if (!(ok = warp_wait(bar(B_FULL + item % NSLOT), (item / NSLOT) & 1))) break;
-          if (key0 + row >= it.k_len) {
-            uint8_t* vrow = gbase + OFF_RING + (item % NSLOT) * kTileBytes + row * 128;
+          if (row < BN && key0 + row >= it.k_len) {
+            uint8_t* vrow = gbase + OFF_RING + (item % NSLOT) * kKVTileBytes + row * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
 #pragma unroll
               for (int hf = 0; hf < kHalves; ++hf)
-                *reinterpret_cast<uint4*>(vrow + hf * kRegion + c * 16) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vrow + hf * kKVRegion + c * 16) = make_uint4(0, 0, 0, 0);
             }
           }
           fence_proxy_async_smem();  // generic stores -> the MMA's async-proxy reads
         }
         tc_fence_before();
-        mbar_arrive(bar(pf));
+        mbar_arrive(bar(B_PF + tq * SBUF + sbuf));
       }
       items += 2 * it.n_all;
       if (!ok) break;
@@ -870,16 +926,16 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   int page_shift = 0, box_rows = 0;
   if (p.paged) {
     while ((1 << page_shift) < p.page) ++page_shift;
-    box_rows = p.page < BN ? p.page : BN;
+    box_rows = p.page < BN ? p.page : BN;  // whole pages, at most one key tile per box
     rc = make_page_map(&mk, p.k, p.kt, p.DQ, p.HK, p.page, p.k_pages, p.ks0, p.ks1, p.ks2, box_rows);
     if (rc) return rc;
     rc = make_page_map(&mv, p.v, p.vt, p.DV, p.HK, p.page, p.k_pages, p.vs0, p.vs1, p.vs2, box_rows);
     if (rc) return rc;
   } else {
     if (p.k_rows <= 0) return fail(FA_ERR_INVALID, "prefill needs packed K/V rows");
-    rc = make_map(&mk, p.k, p.kt, p.DQ, p.k_rows, p.HK, p.ks1, p.ks2);
+    rc = make_map(&mk, p.k, p.kt, p.DQ, p.k_rows, p.HK, p.ks1, p.ks2, BN);
     if (rc) return rc;
-    rc = make_map(&mv, p.v, p.vt, p.DV, p.k_rows, p.HK, p.vs1, p.vs2);
+    rc = make_map(&mv, p.v, p.vt, p.DV, p.k_rows, p.HK, p.vs1, p.vs2, BN);
     if (rc) return rc;
   }
   CUtensorMap mo;  // output tile stores: 32 rows x 64 head dims per box
