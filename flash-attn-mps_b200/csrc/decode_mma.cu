@@ -572,6 +572,12 @@ int page_shift_of(const AttnParams& p) {
 #ifndef FAB_DECODE_16_MIN_SPLITS
 #define FAB_DECODE_16_MIN_SPLITS 4
 #endif
+#ifndef FAB_DECODE_16_SLOT_FILL  // target CTAs per resident slot x 10 (16-bit, grid below the slots)
+#define FAB_DECODE_16_SLOT_FILL 8
+#endif
+#ifndef FAB_DECODE_16_MIN_SPLITS_SMALL
+#define FAB_DECODE_16_MIN_SPLITS_SMALL 1
+#endif
 #ifndef FAB_DECODE_TMA
 #define FAB_DECODE_TMA 1
 #endif
@@ -690,11 +696,13 @@ int decode_default_splits(const AttnParams& p, int* span) {
   } else {
     // When one split per (request, KV head) already fills the resident CTA
     // slots, 4 splits keep a ragged batch from ending on its longest request
-    // (config 3: 6.83 TB/s vs 6.22 with 1); otherwise about 1.7 CTAs per slot
-    // (64 x 1152..16384 tokens: 2 splits beat 3 and 4 by 3-13%).
+    // (config 3: 6.84 TB/s; 2 splits 6.64); otherwise enough splits for ~0.8
+    // CTAs per slot, all resident at once without a second partial wave (64
+    // requests x 1152 / 2048 / 4096 / 16384 tokens: 1 split 5.62 / 6.10 /
+    // 6.43 / 6.99 TB/s against 4.32 / 5.18 / 6.03 / 6.80 with 2).
     const int64_t slots = (int64_t)sm_count() * FAB_DECODE_16_MINB;
-    const int want = (int)((17 * slots + 10 * units - 1) / (10 * units));
-    splits = max(want, units >= slots ? FAB_DECODE_16_MIN_SPLITS : 2);
+    const int want = (int)((FAB_DECODE_16_SLOT_FILL * slots + 10 * units - 1) / (10 * units));
+    splits = max(want, units >= slots ? FAB_DECODE_16_MIN_SPLITS : FAB_DECODE_16_MIN_SPLITS_SMALL);
   }
   splits = max(1, min(splits, by_len));
   *span = (eff + splits - 1) / splits;
