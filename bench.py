@@ -16,7 +16,7 @@ with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
 that token, attention, D2H of the output.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_decode|prefill|prefill_softcap_window|bf16_decode|serving]
+                    [--workload fp8_decode|prefill|prefill_softcap_window|prefill_fp8kv|bf16_decode|serving]
                     [--attention-path fused|native] [--small]
 """
 
@@ -374,10 +374,16 @@ def time_loop(fn, steps, warmup):
     return s.elapsed_time(e) / steps
 
 
-def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False):
-    """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func."""
+def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False):
+    """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
+
+    ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
+    descales through the vLLM entry (vLLM's FP8 KV-cache prefill), which runs
+    on the mma.sync tensor-core kernel.
+    """
     import torch
     from flash_attn_b200 import flash_attn_varlen_func
+    from flash_attn_b200.vllm import flash_attn_varlen_func as vllm_varlen
     cfg = dict(CFG2)
     if small:
         cfg["seqs"] = 4  # profiling case
@@ -390,13 +396,22 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     v = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
     cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
-    ms = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
-                                                  softcap=softcap, window_size=window, out=out),
-                   steps, warmup)
+    if fp8_kv:
+        k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+        kd = torch.full((len(lens), cfg["hkv"]), 0.5, device=dev)
+        vd = torch.full((len(lens), cfg["hkv"]), 2.0, device=dev)
+        ms = time_loop(lambda: vllm_varlen(q, k, v, max(lens), cu, max(lens), cu_seqlens_k=cu, causal=True,
+                                           k_descale=kd, v_descale=vd, out=out), steps, warmup)
+    else:
+        ms = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
+                                                      softcap=softcap, window_size=window, out=out),
+                       steps, warmup)
     flops = cfg2_flops(lens, cfg, window[0])
     tflops = flops / (ms * 1e-3) / 1e12
     return {"workload": "cfg2: varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
-                        + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else ""),
+                        + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else "")
+                        + (", FP8 E4M3 K/V with descales (mma.sync kernel)" if fp8_kv else "")
+                        + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "TFLOP/s": tflops,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
@@ -664,8 +679,8 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "bf16_decode",
-                                           "serving"],
+    ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
+                                           "bf16_decode", "serving"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -701,6 +716,9 @@ def main():
                           "dtype": "bf16", "data": "synthetic (seeded random weights and prompts)"})
                 print(json.dumps(r))
                 return
+            elif args.workload == "prefill_fp8kv":
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
             elif args.workload == "prefill_softcap_window":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, softcap=50.0,
                                 window=(1024, 0), small=args.small)
@@ -711,7 +729,8 @@ def main():
             print(json.dumps({"metric": METRIC, "value": value, "unit": unit, "n_gpus": 1,
                               "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
                               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-                              "dtype": "bf16", "data": "synthetic (seeded)",
+                              "dtype": "bf16 q, fp8_e4m3 K/V" if args.workload == "prefill_fp8kv" else "bf16",
+                              "data": "synthetic (seeded)",
                               "config": {"workload": r["workload"]}, "roofline": r["roofline"]}))
         return
     res = run_fp8_decode(args, rank, world, peaks, peak_kind)
@@ -727,6 +746,7 @@ def main():
                 "prefill_cfg2": rested(lambda: run_prefill(peaks, peak_kind)),
                 "prefill_cfg2_softcap_window": rested(lambda: run_prefill(peaks, peak_kind, softcap=50.0,
                                                                           window=(1024, 0))),
+                "prefill_cfg2_fp8kv": rested(lambda: run_prefill(peaks, peak_kind, steps=10, warmup=3, fp8_kv=True)),
                 "decode_cfg3": rested(lambda: run_bf16_decode(peaks, peak_kind)),
                 "serving_cfg5": run_serving(peaks, peak_kind)}
         if world == 1 and not args.no_cpu_baseline and not args.small:
