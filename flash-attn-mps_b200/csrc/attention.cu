@@ -90,7 +90,23 @@ int encode_tensor_map(void* map, int dtype, int rank, const void* ptr, const uin
 
 namespace {
 
-enum Route { kRouteGeneric = 0, kRouteDecode = 1, kRoutePrefill = 2, kRouteMma = 3 };
+enum Route { kRouteGeneric = 0, kRouteDecode = 1, kRoutePrefill = 2, kRouteMma = 3, kRouteFp8Prefill = 4 };
+
+// Workspace of the FP8 prefill route: work counter, 16-bit K and V copies,
+// then (paged K/V) row starts [B+1] and lengths [B].
+struct Fp8Layout {
+  size_t kv_off, kv_bytes, cu_off, used_off, total;
+};
+Fp8Layout fp8_layout(const AttnParams& p) {
+  auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+  Fp8Layout l{};
+  l.kv_off = 256;
+  l.kv_bytes = up((size_t)fp8_prefill_rows(p) * p.HK * p.DQ * 2);
+  l.cu_off = l.kv_off + 2 * l.kv_bytes;
+  l.used_off = l.cu_off + up((size_t)(p.B + 1) * 4);
+  l.total = l.used_off + up((size_t)p.B * 4);
+  return l;
+}
 
 struct Plan {
   int route;
@@ -258,10 +274,20 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
       plan->splits = a->num_splits > 0 ? a->num_splits : std::max(1, std::min(32, (eff + 255) / 256));
     }
   } else {
+    AttnParams view;
     if (a->num_splits == 0 && prefill_sm100_supported(p)) {
       plan->route = kRoutePrefill;
       plan->splits = 1;
       plan->part_bytes = 256;  // persistent-scheduler work counter
+      return FA_OK;
+    } else if (a->num_splits == 0 && a->max_seqlen_q >= 128 && fp8_prefill_view(p, &view)) {
+      // FP8 K/V with at least one full 128-row query tile: an exact 16-bit
+      // copy of the K/V rows (3 bytes per element of extra traffic) turns the
+      // call into the tcgen05 prefill's compute-bound work; shorter query
+      // chunks stay on the mma.sync kernel, which reads the FP8 bytes directly.
+      plan->route = kRouteFp8Prefill;
+      plan->splits = 1;
+      plan->part_bytes = fp8_layout(p).total;
       return FA_OK;
     } else {
       const bool vector = a->max_seqlen_q == 1 || std::max(p.DQ, p.DV) > 256;
@@ -331,11 +357,32 @@ extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
   rc = make_plan(a, p, &plan);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (plan.route == kRoutePrefill) {
+  if (plan.route == kRoutePrefill || plan.route == kRouteFp8Prefill) {
     FAB_CHECK_ARG(present(a->workspace) && a->workspace.ndim >= 1 &&
                       (size_t)a->workspace.shape[0] * elem_size(a->workspace.dtype) >= plan.part_bytes,
                   "workspace smaller than fa_attention_workspace_size");
+    FAB_CHECK_ARG(((uintptr_t)a->workspace.ptr & 255u) == 0 || plan.route == kRoutePrefill,
+                  "workspace must be 256-byte aligned");
     p.scratch = a->workspace.ptr;
+  }
+  if (plan.route == kRouteFp8Prefill) {
+    AttnParams view;
+    if (!fp8_prefill_view(p, &view)) return fail(FA_ERR_INVALID, "FP8 prefill plan no longer applies");
+    const Fp8Layout l = fp8_layout(p);
+    uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace.ptr);
+    int32_t* cu_out = p.paged ? reinterpret_cast<int32_t*>(ws + l.cu_off) : nullptr;
+    int32_t* used_out = p.paged ? reinterpret_cast<int32_t*>(ws + l.used_off) : nullptr;
+    rc = launch_kv_dequant(p, ws + l.kv_off, ws + l.kv_off + l.kv_bytes, cu_out, used_out, st);
+    if (rc) return rc;
+    view.k = ws + l.kv_off;
+    view.v = ws + l.kv_off + l.kv_bytes;
+    if (p.paged) {
+      view.cu_k = cu_out; view.ck0 = 1;
+      view.used = used_out; view.u0 = 1;
+    }
+    view.scratch = ws;
+    view.splits = 1;
+    return launch_prefill_sm100(view, st);
   }
   if (plan.splits > 1) {
     FAB_CHECK_ARG(present(a->workspace) && a->workspace.ndim >= 1 &&

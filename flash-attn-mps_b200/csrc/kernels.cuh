@@ -75,6 +75,13 @@ int prefill_sm100_supported(const AttnParams& p);
 int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream);
 int mma_attention_supported(const AttnParams& p);
 int launch_mma_attention(const AttnParams& p, cudaStream_t stream);
+// FP8 E4M3 K/V prefill on the tcgen05 kernel through an exact 16-bit copy of
+// the K/V rows (kv_dequant.cu): rows of that copy, the prefill's view of it
+// (false when the prefill cannot take it), and the conversion launch.
+int64_t fp8_prefill_rows(const AttnParams& p);
+bool fp8_prefill_view(const AttnParams& p, AttnParams* view);
+int launch_kv_dequant(const AttnParams& p, void* k_out, void* v_out, int32_t* cu_out, int32_t* used_out,
+                      cudaStream_t stream);
 // Timed-out pipeline waits recorded by the prefill / TMA decode kernels on the
 // current device (1 = some wait gave up, 0 = none, -1 = CUDA error).
 int prefill_timeout_flag(bool clear);
