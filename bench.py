@@ -374,12 +374,15 @@ def time_loop(fn, steps, warmup):
     return s.elapsed_time(e) / steps
 
 
-def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False):
+def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False,
+                kv_slice=None):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
 
     ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
-    descales through the vLLM entry (vLLM's FP8 KV-cache prefill), which runs
-    on the mma.sync tensor-core kernel.
+    descales through the vLLM entry (vLLM's FP8 KV-cache prefill): an exact
+    16-bit copy of the K/V rows, then the tcgen05 prefill.
+    ``kv_slice=(h0, h1)``: only KV heads [h0, h1) and their query heads (one
+    GPU's share when the prefill is sharded by head groups).
     """
     import torch
     from flash_attn_b200 import flash_attn_varlen_func
@@ -394,6 +397,12 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     q = torch.randn(total, cfg["hq"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
     k = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
     v = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
+    if kv_slice is not None:
+        group = cfg["hq"] // cfg["hkv"]
+        h0, h1 = kv_slice
+        q = q[:, h0 * group:h1 * group].contiguous()
+        k, v = k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous()
+        cfg["hq"], cfg["hkv"] = (h1 - h0) * group, h1 - h0
     cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=dev)
     out = torch.empty_like(q)
     if fp8_kv:
@@ -410,7 +419,8 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     tflops = flops / (ms * 1e-3) / 1e12
     return {"workload": "cfg2: varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
                         + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else "")
-                        + (", FP8 E4M3 K/V with descales (mma.sync kernel)" if fp8_kv else "")
+                        + (", FP8 E4M3 K/V with descales (16-bit copy + tcgen05 prefill)" if fp8_kv else "")
+                        + (f", KV heads {kv_slice[0]}..{kv_slice[1] - 1} only" if kv_slice else "")
                         + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "TFLOP/s": tflops,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
@@ -613,6 +623,34 @@ def run_serving(peaks, peak_kind, steps=2, warmup=3, small=False, path="fused", 
     return line
 
 
+def multi_gpu_secondary(rank, world, peaks, peak_kind):
+    """Configs 2 and 3 at N > 1, where they shard with no communication:
+    config-2 prefill split by KV-head groups (each rank takes HKV/N KV heads
+    and their query heads) and config-3 decode as one full replica per GPU.
+    Whole-job aggregates over the max-over-ranks device time."""
+    out = {}
+    hkv = CFG2["hkv"]
+    if hkv % world == 0:
+        per = hkv // world
+        barrier(world)
+        r = run_prefill(peaks, peak_kind, kv_slice=(rank * per, (rank + 1) * per))
+        ms = max_over_ranks(r["ms_per_step"], world)
+        flops = r["tflop_per_step"] * world * 1e12  # equal head shares
+        out["prefill_cfg2_head_sharded"] = {
+            "workload": f"cfg2 prefill, {per} KV head(s) + {per * CFG2['hq'] // hkv} query heads per GPU, no communication",
+            "ms_per_step": ms, "TFLOP/s": flops / (ms * 1e-3) / 1e12,
+            "per_gpu_TFLOP/s": flops / world / (ms * 1e-3) / 1e12}
+    barrier(world)
+    r = run_bf16_decode(peaks, peak_kind)
+    ms = max_over_ranks(r["ms_per_step"], world)
+    out["decode_cfg3_replicas"] = {
+        "workload": "cfg3 paged bf16 decode, one full replica per GPU, no communication",
+        "ms_per_step": ms, "TB/s": world * r["bytes_per_step"] / (ms * 1e-3) / 1e12,
+        "per_gpu_TB/s": r["bytes_per_step"] / (ms * 1e-3) / 1e12}
+    barrier(world)
+    return out
+
+
 # ------------------------------------------------------------------ CPU legs
 def cpu_fp8_decode_sample(cfg, requests=1, seed=4):
     """The oracle (reference CPU math, float64) on a bounded sample of config 4."""
@@ -734,6 +772,8 @@ def main():
                               "config": {"workload": r["workload"]}, "roofline": r["roofline"]}))
         return
     res = run_fp8_decode(args, rank, world, peaks, peak_kind)
+    multi = (multi_gpu_secondary(rank, world, peaks, peak_kind)
+             if world > 1 and not args.no_secondary and not args.small else None)
     if rank == 0:
         line = {"metric": METRIC, "value": res["value"], "unit": res["unit"], "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
@@ -749,6 +789,8 @@ def main():
                 "prefill_cfg2_fp8kv": rested(lambda: run_prefill(peaks, peak_kind, steps=10, warmup=3, fp8_kv=True)),
                 "decode_cfg3": rested(lambda: run_bf16_decode(peaks, peak_kind)),
                 "serving_cfg5": run_serving(peaks, peak_kind)}
+        if multi:
+            line["secondary"] = multi
         if world == 1 and not args.no_cpu_baseline and not args.small:
             line["cpu_baseline"] = cpu_baseline_block(CFG4)
         print(json.dumps(line))
