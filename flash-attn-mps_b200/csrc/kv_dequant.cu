@@ -15,6 +15,13 @@
 #include "kernels.cuh"
 #include "ptx.cuh"
 
+#ifndef FAB_FP8_PREFILL_MAX_COPY
+// Largest 16-bit K+V copy (bytes) the route allocates in the workspace; larger
+// calls (long paged contexts x many requests) keep reading the FP8 bytes on
+// the mma.sync kernel instead of asking the caller for gigabytes per call.
+#define FAB_FP8_PREFILL_MAX_COPY (4LL << 30)
+#endif
+
 namespace fab {
 namespace {
 
@@ -116,6 +123,7 @@ bool fp8_prefill_view(const AttnParams& p, AttnParams* view) {
   if (p.paged && (p.page <= 0 || p.k_pages <= 0 || p.bt_cols <= 0)) return false;
   const int64_t rows = fp8_prefill_rows(p);
   if (rows <= 0 || rows >= (1 << 30)) return false;
+  if (2 * rows * p.HK * p.DQ * 2 > (int64_t)FAB_FP8_PREFILL_MAX_COPY) return false;
   AttnParams v = p;
   v.kt = v.vt = p.qt;
   v.ks0 = v.vs0 = 0;

@@ -120,3 +120,27 @@ def test_page_outside_cache_reads_as_zeros(device):
     ref, refl = reference(q, kz, vz, cq, used_k=used, block_table=table, causal=True)
     assert_attention_close(out, ref, torch.bfloat16)
     assert_lse_close(lse, refl)
+
+
+def test_oversized_copy_falls_back_to_mma(device):
+    # max_seqlen_k bounds the paged copy (B * max_k rows): past the copy-size
+    # cap the call stays on the mma.sync kernel, which reads the FP8 bytes.
+    g = torch.Generator().manual_seed(85)
+    page, klens = 16, [100, 37]
+    keys = [torch.randn(n, 2, 128, generator=g).to(torch.float8_e4m3fn) for n in klens]
+    vals = [torch.randn(n, 2, 128, generator=g).to(torch.float8_e4m3fn) for n in klens]
+    kc, table = _paged(keys, page, g, device, 2, 128)
+    vc = torch.zeros_like(kc).cpu()
+    for b, r in enumerate(vals):
+        for i in range(r.shape[0]):
+            vc[table[b, i // page].item(), i % page] = r[i]
+    vc = vc.to(device)
+    q = torch.randn(300, 8, 128, generator=g).to(torch.bfloat16).to(device)
+    cq = cu([150, 150], device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    (out, lse), n = _launches(lambda: vllm_attention(q, kc, vc, 150, cq, 1 << 26, seqused_k=used, block_table=table,
+                                                      causal=True, return_softmax_lse=True))
+    assert n == 1, "expected the mma.sync kernel past the copy-size cap"
+    ref, refl = reference(q, kc, vc, cq, used_k=used, block_table=table, causal=True)
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
