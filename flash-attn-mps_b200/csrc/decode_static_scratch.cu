@@ -17,10 +17,13 @@
 //     FA_ERR_INVALID before anything is launched (lower num_splits, or use
 //     fa_attention_fwd with a caller workspace).
 //   * All calls on a device share the one array and it keeps the previous
-//     call's contents. Nothing in it needs to start at zero: every split of
+//     call's contents. The split partials need no clearing: every split of
 //     every (token, head) writes its partial output and LSE before the merge
-//     reads them. Calls whose GPU work overlaps (different streams without
-//     ordering, or concurrent host threads on different streams) race on it.
+//     reads them. The one value that must start at zero -- the work counter of
+//     the persistent tensor-core kernel, which a num_splits == 1 (batch-
+//     invariant) call runs -- is zeroed on the stream by that launch itself.
+//     Calls whose GPU work overlaps (different streams without ordering, or
+//     concurrent host threads on different streams) race on the array.
 //   * The first call on a device resolves the array's device address with
 //     cudaGetSymbolAddress (this may load the module on that device); make
 //     that first call before any stream capture begins.
