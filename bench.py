@@ -16,7 +16,7 @@ with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
 that token, attention, D2H of the output.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_decode|prefill|prefill_softcap_window|prefill_fp8kv|bf16_decode|serving]
+                    [--workload fp8_decode|prefill|prefill_softcap_window|prefill_fp8kv|prefill_alibi|bf16_decode|serving]
                     [--attention-path fused|native] [--small]
 """
 
@@ -375,7 +375,7 @@ def time_loop(fn, steps, warmup):
 
 
 def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False,
-                kv_slice=None):
+                kv_slice=None, alibi=False):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
 
     ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
@@ -383,6 +383,7 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     16-bit copy of the K/V rows, then the tcgen05 prefill.
     ``kv_slice=(h0, h1)``: only KV heads [h0, h1) and their query heads (one
     GPU's share when the prefill is sharded by head groups).
+    ``alibi``: the standard geometric ALiBi slopes 2^(-8(h+1)/H) per query head.
     """
     import torch
     from flash_attn_b200 import flash_attn_varlen_func
@@ -412,8 +413,11 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
         ms = time_loop(lambda: vllm_varlen(q, k, v, max(lens), cu, max(lens), cu_seqlens_k=cu, causal=True,
                                            k_descale=kd, v_descale=vd, out=out), steps, warmup)
     else:
+        slopes = (torch.tensor([2.0 ** (-8.0 * (h + 1) / cfg["hq"]) for h in range(cfg["hq"])], device=dev)
+                  if alibi else None)
         ms = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
-                                                      softcap=softcap, window_size=window, out=out),
+                                                      softcap=softcap, window_size=window, alibi_slopes=slopes,
+                                                      out=out),
                        steps, warmup)
     flops = cfg2_flops(lens, cfg, window[0])
     tflops = flops / (ms * 1e-3) / 1e12
@@ -421,6 +425,7 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
                         + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else "")
                         + (", FP8 E4M3 K/V with descales (16-bit copy + tcgen05 prefill)" if fp8_kv else "")
                         + (f", KV heads {kv_slice[0]}..{kv_slice[1] - 1} only" if kv_slice else "")
+                        + (", ALiBi slopes" if alibi else "")
                         + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "TFLOP/s": tflops,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
@@ -718,7 +723,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
-                                           "bf16_decode", "serving"],
+                                           "prefill_alibi", "bf16_decode", "serving"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -754,6 +759,9 @@ def main():
                           "dtype": "bf16", "data": "synthetic (seeded random weights and prompts)"})
                 print(json.dumps(r))
                 return
+            elif args.workload == "prefill_alibi":
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, alibi=True)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
             elif args.workload == "prefill_fp8kv":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)
                 value, unit = r["TFLOP/s"], "TFLOP/s"

@@ -275,7 +275,8 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
     }
   } else {
     AttnParams view;
-    if (a->num_splits == 0 && prefill_sm100_supported(p)) {
+    // (Single-query ALiBi calls keep the split-KV route of the kernels below.)
+    if (a->num_splits == 0 && prefill_sm100_supported(p) && !(p.alibi && a->max_seqlen_q == 1)) {
       plan->route = kRoutePrefill;
       plan->splits = 1;
       plan->part_bytes = 256;  // persistent-scheduler work counter

@@ -128,6 +128,7 @@ struct PrefillParams {
   int* counter;                           // work counter, zero at launch
   const int32_t* table; int64_t bt0, bt1;  // paged K/V: block_table [B, bt_cols] (null for packed K/V)
   int32_t bt_cols, page_shift, box_rows;   // page = 1 << page_shift tokens, box_rows = min(page, 128)
+  const float* alibi; int64_t al0, al1;    // ALiBi slopes [B,H] or [H] (ALIBI instantiation only)
   int32_t B, HQ, HK, n_pairs, causal, win_l, win_r;
   float scale, softcap;
 };
@@ -360,12 +361,14 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
 }
 
 // HDIM: head dim (64 or 128) = number of 64-element swizzle regions x 64.
-template <bool BF16, bool SOFTCAP, int HDIM>
+// ALIBI: scores minus slope * |q_abs - key| (not combined with a softcap).
+template <bool BF16, bool SOFTCAP, int HDIM, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
                          const PrefillParams p) {
   static_assert(HDIM == 64 || HDIM == 128, "head dim");
+  static_assert(!(SOFTCAP && ALIBI), "softcap with ALiBi runs on the mma.sync kernel");
   constexpr int kHalves = HDIM / 64;             // 64-element regions per row
   constexpr int kLoadBytes = kHalves * kRegion;      // bytes of one Q tile actually loaded
   constexpr int kKVLoadBytes = kHalves * kKVRegion;  // bytes of one K/V tile actually loaded
@@ -639,6 +642,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int h = it.h;
       const float qk_scale = it.qk_scale, vscale = it.vscale;
       const float sl2 = qk_scale * 1.4426950408889634f;     // raw score -> log2 units
+      // ALiBi slope in log2 units; with ALiBi the scores are biased (and thus
+      // already in log2 units) before the row max, so the exp stage scales by 1.
+      const float slope_l2 = ALIBI ? p.alibi[it.b * p.al0 + (int64_t)h * p.al1] * 1.4426950408889634f : 0.f;
+      const float sl2e = ALIBI ? 1.f : sl2;
       const float cap_l2 = p.softcap * 1.4426950408889634f;  // softcap: cap*log2e*tanh(s*scale/cap)
       const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
       // Running max in log2 units; a sink acts as one extra logit with zero value.
@@ -667,6 +674,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < BN; ++i)
             if (i < c_lo || i > c_hi) r[i] = __float_as_uint(-INFINITY);
         }
+        if constexpr (ALIBI) {
+          // v = s*scale*log2e - slope*log2e*|q_abs - key| (the reference's
+          // score minus the ALiBi bias, in log2 units); masked scores stay -inf.
+          const float base = (float)(q_abs - key0);
+          const uint64_t sl2x2a = f2pack(sl2, sl2), nslope2 = f2pack(-slope_l2, -slope_l2);
+#pragma unroll
+          for (int i = 0; i < BN; i += 2) {
+            const uint64_t d2 = f2pack(fabsf(base - (float)i), fabsf(base - (float)(i + 1)));
+            const uint64_t t2 = fmul2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sl2x2a);
+            float v0, v1;
+            f2unpack(ffma2(d2, nslope2, t2), v0, v1);
+            r[i] = __float_as_uint(v0);
+            r[i + 1] = __float_as_uint(v1);
+          }
+        }
         // Row max as 8 independent 3-input max chains (exact in any order).
         float mx8[8];
 #pragma unroll
@@ -677,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         // scale > 0 and tanh is increasing: the max commutes with both.
-        const float m_tile = SOFTCAP ? (mx == -INFINITY ? -INFINITY : cap_l2 * tanh_id(mx * cap_in)) : mx * sl2;
+        const float m_tile = SOFTCAP ? (mx == -INFINITY ? -INFINITY : cap_l2 * tanh_id(mx * cap_in)) : mx * sl2e;
         float factor = 1.f;
         if (m_tile > m_run + kRescaleThreshold || (m_run == -INFINITY && m_tile != -INFINITY)) {
           factor = m_run == -INFINITY ? 0.f : ex2(m_run - m_tile);
@@ -691,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t ls2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
-        const uint64_t sl2x2 = f2pack(sl2, sl2), nmsub2 = f2pack(-msub, -msub);
+        const uint64_t sl2x2 = f2pack(sl2e, sl2e), nmsub2 = f2pack(-msub, -msub);
         // softcap constants: e^(2y) = 2^(s * cap_in * 2 log2e)
         const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
         const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
@@ -894,7 +916,8 @@ int prefill_sm100_supported(const AttnParams& p) {
     for (int64_t v : ps)
       if (v <= 0 || (v * 2) % 16 != 0) return 0;
   }
-  if (p.alibi || p.mask || p.leftpad || p.cp_n > 1) return 0;
+  if (p.mask || p.leftpad || p.cp_n > 1) return 0;
+  if (p.alibi && p.softcap > 0.f) return 0;  // softcap + ALiBi: mma.sync kernel
   if (p.sinks && !(p.sink_t == FA_F32 || p.sink_t == FA_F16 || p.sink_t == FA_BF16)) return 0;
   if (p.qs2 != 1 || p.ks3 != 1 || p.vs3 != 1 || p.os2 != 1) return 0;
   if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !al16(p.out)) return 0;
@@ -963,11 +986,15 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.win_l = p.win_l; pp.win_r = p.win_r;
   pp.scale = p.scale;
   pp.softcap = p.softcap;
-  const bool cap = p.softcap > 0.f;
+  pp.alibi = p.alibi; pp.al0 = p.a0; pp.al1 = p.a1;
+  const bool cap = p.softcap > 0.f, alibi = p.alibi != nullptr;
   auto pick = [&](auto hd) {
     constexpr int H = decltype(hd)::value;
-    return p.qt == FA_BF16 ? (cap ? prefill_sm100_kernel<true, true, H> : prefill_sm100_kernel<true, false, H>)
-                           : (cap ? prefill_sm100_kernel<false, true, H> : prefill_sm100_kernel<false, false, H>);
+    if (p.qt == FA_BF16)
+      return cap ? prefill_sm100_kernel<true, true, H, false>
+                 : alibi ? prefill_sm100_kernel<true, false, H, true> : prefill_sm100_kernel<true, false, H, false>;
+    return cap ? prefill_sm100_kernel<false, true, H, false>
+               : alibi ? prefill_sm100_kernel<false, false, H, true> : prefill_sm100_kernel<false, false, H, false>;
   };
   auto kernel = p.DQ == 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 128>{});
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);

@@ -61,7 +61,7 @@ def test_head_dims_and_diffkv(device, dims, causal):
     qlens, klens = [1, 65, 200], [40, 65, 333]
     q, k, v = _qkv(device, torch.bfloat16, qlens, klens, 8, 4, dims[0], dims[1], seed=3)
     cq, ck = cu(qlens, device), cu(klens, device)
-    # ALiBi keeps head dim 64 off the tcgen05 path too.
+    # Head dim 64 with ALiBi (taken by the tcgen05 kernel since it gained ALiBi).
     slopes = torch.linspace(.01, .1, 8, device=device) if dims == (64, 64) else None
     out, lse = flash_attn_varlen_func(q, k, v, cq, ck, max(qlens), max(klens), causal=causal,
                                       alibi_slopes=slopes, return_softmax_lse=True)
