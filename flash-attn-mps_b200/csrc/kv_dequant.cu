@@ -114,7 +114,7 @@ int64_t fp8_prefill_rows(const AttnParams& p) {
 
 bool fp8_prefill_view(const AttnParams& p, AttnParams* view) {
   if (p.kt != FA_E4M3 || p.vt != FA_E4M3 || !(p.qt == FA_BF16 || p.qt == FA_F16)) return false;
-  if (p.DQ != p.DV || (p.DQ != 64 && p.DQ != 128)) return false;
+  if (p.DQ != p.DV || p.DQ % 16 || p.DQ < 16 || p.DQ > 128) return false;
   if (p.ks3 != 1 || p.vs3 != 1 || p.max_k <= 0 || p.HK <= 0) return false;
   if (((uintptr_t)p.k & 15u) || ((uintptr_t)p.v & 15u)) return false;
   const int64_t st[6] = {p.paged ? p.ks0 : 16, p.ks1, p.ks2, p.paged ? p.vs0 : 16, p.vs1, p.vs2};

@@ -129,6 +129,7 @@ struct PrefillParams {
   const int32_t* table; int64_t bt0, bt1;  // paged K/V: block_table [B, bt_cols] (null for packed K/V)
   int32_t bt_cols, page_shift, box_rows;   // page = 1 << page_shift tokens, box_rows = min(page, 128)
   const float* alibi; int64_t al0, al1;    // ALiBi slopes [B,H] or [H] (ALIBI instantiation only)
+  int32_t dim;                             // true head dim (<= HDIM; columns past it are TMA zero fill)
   int32_t B, HQ, HK, n_pairs, causal, win_l, win_r;
   float scale, softcap;
 };
@@ -854,7 +855,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (staged) {
             const int chunk = (c & 1) * 4 + v;
             *reinterpret_cast<uint4*>(stg + (c >> 1) * 4096 + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = val;
-          } else if (row_ok) {
+          } else if (row_ok && c * 32 + v * 8 < p.dim) {
             *reinterpret_cast<uint4*>(orow + (c * 32 + v * 8) * 2) = val;
           }
         }
@@ -906,7 +907,11 @@ bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
 int prefill_sm100_supported(const AttnParams& p) {
   if (!(p.qt == FA_BF16 || p.qt == FA_F16) || p.kt != p.qt || p.vt != p.qt || p.ot != p.qt) return 0;
-  if (p.DQ != p.DV || (p.DQ != 64 && p.DQ != 128)) return 0;
+  // Head dims up to 128 in multiples of 8 (16-byte rows): the 64- or 128-wide
+  // instantiation runs them, the tensor maps' true extent zero-fills the
+  // padded columns on loads (adding nothing to Q K^T; V's give O columns that
+  // are never stored) and clips them on the tile stores.
+  if (p.DQ != p.DV || p.DQ < 8 || p.DQ > 128 || p.DQ % 8) return 0;
   if (p.paged) {
     // Paged K/V: power-of-two pages of >= 8 tokens (whole 1024-byte swizzle
     // atoms per box), a page stride TMA can address.
@@ -987,6 +992,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   pp.scale = p.scale;
   pp.softcap = p.softcap;
   pp.alibi = p.alibi; pp.al0 = p.a0; pp.al1 = p.a1;
+  pp.dim = p.DV;
   const bool cap = p.softcap > 0.f, alibi = p.alibi != nullptr;
   auto pick = [&](auto hd) {
     constexpr int H = decltype(hd)::value;
@@ -996,7 +1002,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
     return cap ? prefill_sm100_kernel<false, true, H, false>
                : alibi ? prefill_sm100_kernel<false, false, H, true> : prefill_sm100_kernel<false, false, H, false>;
   };
-  auto kernel = p.DQ == 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 128>{});
+  auto kernel = p.DQ <= 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 128>{});
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return fail(FA_ERR_CUDA, "prefill smem attribute: %s", cudaGetErrorString(e));
   // The warpgroups' setmaxnreg split assumes exactly kLaunchRegs registers per
