@@ -119,8 +119,9 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
 #pragma unroll
       for (int khalf = 0; khalf < 2; ++khalf) {
         const int d = FP8 ? kk * 16 + 4 * qd + 2 * khalf : kk * 16 + 8 * khalf + 2 * qd;
-        float x0 = ok ? load_float(p.q, p.qt, base + d * p.qs2) : 0.f;
-        float x1 = ok ? load_float(p.q, p.qt, base + (d + 1) * p.qs2) : 0.f;
+        // Head dims below D (the instantiation) read as zero past the true dim.
+        float x0 = ok && d < p.DQ ? load_float(p.q, p.qt, base + d * p.qs2) : 0.f;
+        float x1 = ok && d + 1 < p.DQ ? load_float(p.q, p.qt, base + (d + 1) * p.qs2) : 0.f;
         if (QFOLD) { x0 *= scale; x1 *= scale; }
         qb[n8][kk][khalf] = pack2<MT>(x0, x1);
       }
@@ -194,8 +195,9 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
         }
       }
       const uint32_t o = G::off(r, c);
-      cp_async_16(smem_u32(ks) + o, kglob + koff * elt + c * 16, ok ? 16 : 0);
-      cp_async_16(smem_u32(vs) + o, vglob + voff * elt + c * 16, ok ? 16 : 0);
+      const bool col = c * 16 < p.DQ * elt;  // 16-byte chunks past the true head dim are zero-filled
+      cp_async_16(smem_u32(ks) + o, kglob + koff * elt + c * 16, ok && col ? 16 : 0);
+      cp_async_16(smem_u32(vs) + o, vglob + voff * elt + c * 16, ok && col ? 16 : 0);
     }
   };
 
@@ -503,6 +505,7 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
 #pragma unroll 4
     for (int i = 0; i < kPer; ++i) {
       const int d = dbase + i;
+      if (d >= p.DV) break;
       float v = 0.f;
 #pragma unroll
       for (int w = 0; w < W; ++w) v += wgt[w] * co[(w * NH + hcol) * D + d];
@@ -510,10 +513,11 @@ __global__ void __launch_bounds__((W + (TMA ? 1 : 0)) * 32, MINB)
     }
     if (tid % kThreadsPerHead == 0) p.lse[(int64_t)h * p.ls0 + (int64_t)token * p.ls1] = lse;
   } else {
-    float* dst = p.part + (((int64_t)split * p.T + token) * p.HQ + h) * D;
+    float* dst = p.part + (((int64_t)split * p.T + token) * p.HQ + h) * p.DV;
 #pragma unroll 4
     for (int i = 0; i < kPer; ++i) {
       const int d = dbase + i;
+      if (d >= p.DV) break;
       float v = 0.f;
 #pragma unroll
       for (int w = 0; w < W; ++w) v += wgt[w] * co[(w * NH + hcol) * D + d];
@@ -669,7 +673,11 @@ int decode_mma_supported(const AttnParams& p) {
   const bool fp8 = p.kt == FA_E4M3;
   if (!fp8 && p.kt != p.qt) return 0;
   if (p.DQ != p.DV) return 0;
-  if (fp8 ? p.DQ != 128 : (p.DQ != 64 && p.DQ != 128)) return 0;
+  // Head dims up to 128 (multiples of 8, of 16 for FP8 rows) run on the 64-
+  // or 128-wide instantiation: the tail of Q reads as zero, K/V chunks past the
+  // true dim are zero-filled (TMA out-of-bounds fill or cp.async zero fill) and
+  // only true-dim outputs are written.
+  if (p.DQ < 8 || p.DQ > 128 || p.DQ % (fp8 ? 16 : 8)) return 0;
   if (p.alibi || p.mask != 0) return 0;
   if (p.ks3 != 1 || p.vs3 != 1) return 0;
   const int elt = fp8 ? 1 : 2;
@@ -729,10 +737,10 @@ int launch_decode_mma(const AttnParams& p, int splits, int span, cudaStream_t st
     return launch_heads<__half, true, 128>(p, splits, span, prec, qfold, stream);
   }
   if (p.qt == FA_BF16) {
-    return p.DQ == 64 ? launch_heads<__nv_bfloat16, false, 64>(p, splits, span, prec, false, stream)
+    return p.DQ <= 64 ? launch_heads<__nv_bfloat16, false, 64>(p, splits, span, prec, false, stream)
                       : launch_heads<__nv_bfloat16, false, 128>(p, splits, span, prec, false, stream);
   }
-  return p.DQ == 64 ? launch_heads<__half, false, 64>(p, splits, span, prec, false, stream)
+  return p.DQ <= 64 ? launch_heads<__half, false, 64>(p, splits, span, prec, false, stream)
                     : launch_heads<__half, false, 128>(p, splits, span, prec, false, stream);
 }
 
