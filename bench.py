@@ -172,6 +172,94 @@ def build_fp8_cache(rank, world, cfg, seed=4):
     return k_cache, v_cache, table, ks, vs
 
 
+def cfg4_query(cfg, seed=99):
+    """Config-4 queries [B, Hq, D] bf16 on the host (seeded)."""
+    import torch
+    gq = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(cfg["batch"], cfg["hq"], cfg["d"], generator=gq).to(torch.bfloat16), gq
+
+
+def build_cfg3(cfg):
+    """Config 3 exactly as timed: B requests with contexts ~U[cmin, cmax]
+    (seeded), a bf16 paged cache of N(0,1) rows whose pages come from a seeded
+    random permutation, and N(0,1) queries. Returns a dict of device tensors
+    plus the host-side contexts and pages per request."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(cfg["seed"])
+    ctx = rng.integers(cfg["cmin"], cfg["cmax"] + 1, size=cfg["batch"])
+    P = cfg["page"]
+    pages_per = (ctx + P - 1) // P
+    n_pages = int(pages_per.sum())
+    max_pages = int(pages_per.max())
+    perm = torch.from_numpy(rng.permutation(n_pages).astype(np.int32))
+    table = torch.zeros(cfg["batch"], max_pages, dtype=torch.int32)
+    off = 0
+    for b in range(cfg["batch"]):
+        table[b, :pages_per[b]] = perm[off:off + pages_per[b]]
+        off += pages_per[b]
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    kc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    vc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    q = torch.randn(cfg["batch"], cfg["hq"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
+    return {"q": q, "k_cache": kc, "v_cache": vc, "table": table.to(dev),
+            "used": torch.from_numpy(ctx.astype(np.int32)).to(dev),
+            "cu_q": torch.arange(cfg["batch"] + 1, dtype=torch.int32, device=dev),
+            "ctx": ctx, "pages_per": pages_per}
+
+
+def gather_request(cache, table, b, length, page):
+    """Rows [length, Hkv, D] of request b of a paged cache (device gather)."""
+    n = (length + page - 1) // page
+    return cache[table[b, :n].long()].reshape(-1, *cache.shape[2:])[:length]
+
+
+def torch_decode_reference(q, k_rows, v_rows, k_descale=None, v_descale=None, scale=None):
+    """fp32 single-query attention of one request on the GPU: q [Hq, D],
+    K/V rows [L, Hkv, D] (any float or FP8 dtype), per-KV-head descales.
+    Returns out [Hq, Dv] and natural-log LSE [Hq] in fp32."""
+    import torch
+    hq, d = q.shape
+    hkv = k_rows.shape[1]
+    scale = d ** -0.5 if scale is None else scale
+    k = k_rows.float().permute(1, 0, 2)  # [Hkv, L, D]
+    v = v_rows.float().permute(1, 0, 2)
+    if k_descale is not None:
+        k = k * k_descale.float().reshape(hkv, 1, 1)
+    if v_descale is not None:
+        v = v * v_descale.float().reshape(hkv, 1, 1)
+    qg = q.float().reshape(hkv, hq // hkv, d)
+    s = torch.matmul(qg, k.transpose(1, 2)) * scale  # [Hkv, G, L]
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.matmul(torch.exp(s - lse[..., None]), v)
+    return o.reshape(hq, -1), lse.reshape(hq)
+
+
+def sample_requests(lengths, count=6, seed=0):
+    """Shortest, longest and count-2 further seeded distinct request indices."""
+    import numpy as np
+    lengths = np.asarray(lengths)
+    picked = [int(np.argmin(lengths)), int(np.argmax(lengths))]
+    if picked[0] == picked[1]:
+        picked = [0, len(lengths) - 1]
+    rng = np.random.default_rng(seed)
+    rest = [i for i in rng.permutation(len(lengths)).tolist() if i not in picked]
+    return picked + rest[:max(0, count - 2)]
+
+
+def check_close(out, lse, ref_out, ref_lse, what):
+    """The north-star gate (max-abs 1e-2 on outputs, 1e-3 on LSE) plus a
+    scale-aware one (1 % of the reference's largest output), since long-context
+    decode outputs are small averages."""
+    err = (out.float() - ref_out).abs().max().item()
+    scale = ref_out.abs().max().item()
+    lerr = (lse.float() - ref_lse).abs().max().item()
+    if not (err <= 1e-2 and err <= 1e-2 * scale + 2e-5 and lerr <= 1e-3):
+        raise AssertionError(f"{what}: max-abs {err:.3e} (largest output {scale:.3e}), LSE max-abs {lerr:.3e}")
+    return err, lerr
+
+
 def cfg4_bytes(cfg):
     B, C, HK, D, HQ = cfg["batch"], cfg["ctx"], cfg["hkv"], cfg["d"], cfg["hq"]
     kv = B * C * HK * 2 * D * 1
@@ -204,8 +292,8 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     shard = C // world
     dev = torch.device("cuda")
     k_cache, v_cache, table, ks, vs = build_fp8_cache(rank, world, cfg)
-    gq = torch.Generator(device="cpu").manual_seed(99)
-    q_host = torch.randn(B, HQ, D, generator=gq).to(torch.bfloat16).pin_memory()
+    q_host, gq = cfg4_query(cfg)
+    q_host = q_host.pin_memory()
     q = q_host.to(dev)
     kd = ks.reshape(1, HK).expand(B, HK)
     vd = vs.reshape(1, HK).expand(B, HK)
@@ -293,6 +381,8 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     barrier(world)
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.steps, world)
 
+    parity = cfg4_parity(q, k_cache, v_cache, table, kd, vd, used, cu_q, shard, cfg, world, step, partial)
+
     total_bytes = cfg4_bytes(cfg)
     rank_bytes = total_bytes / world
     value = total_bytes / (ms * 1e-3) / 1e12
@@ -308,20 +398,61 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
                      "frac": achieved_gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)",
                      "traffic": (profiled_traffic("decode_mma_fp8_cfg4.md") / world
                                  if profiled_traffic("decode_mma_fp8_cfg4.md") and not args.small else None),
-                     "traffic_source": "profiles/decode_mma_fp8_cfg4.md (ncu dram__bytes_read+write, small case scaled)",
+                     "traffic_source": "profiles/decode_mma_fp8_cfg4.md (ncu, small case scaled)",
                      "algorithmic_bytes_per_launch": rank_bytes,
                      "kernel_ms": kernel_ms},
         "dtype": "fp8_e4m3 KV / bf16 q, fp32 softmax",
-        "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode, split-KV, KV sharded over ranks"
+        "config": {"workload": "cfg4 long-context FP8 E4M3 paged decode, split-KV"
                                + (" (small profiling case)" if args.small else ""),
                    "batch": B, "context": C, "block_size": cfg["page"], "q_heads": HQ, "kv_heads": HK,
-                   "head_dim": D, "kv_bytes_total": B * C * HK * 2 * D,
-                   "l2": "inputs (17.2 GB cache) larger than L2; no flush needed",
-                   "parallelism": f"kv-seq sharded x{world} + NCCL all-gather + merge"},
+                   "head_dim": D, "l2": "17.2 GB cache > L2, no flush",
+                   "parallelism": f"kv-seq sharded x{world}, NCCL all-gather + merge"},
         "gpu_launches": launches,
         "clocks": clocks,
+        "parity": parity,
     }
     return result
+
+
+def cfg4_parity(q, k_cache, v_cache, table, kd, vd, used, cu_q, shard, cfg, world, step, partial):
+    """Sampled self-check of the timed configuration (outside every timed
+    region): for the first, the last and 4 seeded requests, this rank's fp32
+    partial over its KV shard and the merged bf16 output of a step against a
+    torch fp32 reference computed on the GPU from the same cache bytes."""
+    import torch
+    import torch.distributed as dist
+    from flash_attn_b200._attention import attention
+    B, P = cfg["batch"], cfg["page"]
+    picks = sample_requests([shard] * B)
+    _, part_lse = attention(q, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
+                            max_seqlen_k=shard, block_table=table, k_descale=kd, v_descale=vd, out=partial)
+    merged = step(q)
+    merged_out, merged_lse = merged if isinstance(merged, tuple) else (merged, None)
+    refs_o, refs_l = [], []
+    worst = 0.0
+    for b in picks:
+        k_rows = gather_request(k_cache, table, b, shard, P)
+        v_rows = gather_request(v_cache, table, b, shard, P)
+        ro, rl = torch_decode_reference(q[b], k_rows, v_rows, kd[b], vd[b])
+        err, _ = check_close(partial[b], part_lse[:, b], ro, rl, f"cfg4 request {b} partial")
+        worst = max(worst, err)
+        refs_o.append(ro)
+        refs_l.append(rl)
+    ro = torch.stack(refs_o)  # [S, Hq, D]
+    rl = torch.stack(refs_l)  # [S, Hq]
+    if world > 1:
+        go = [torch.empty_like(ro) for _ in range(world)]
+        gl = [torch.empty_like(rl) for _ in range(world)]
+        dist.all_gather(go, ro)
+        dist.all_gather(gl, rl)
+        gl_t = torch.stack(gl)
+        rl = torch.logsumexp(gl_t, dim=0)
+        ro = sum(torch.exp(gl_t[r] - rl)[..., None] * go[r] for r in range(world))
+    for i, b in enumerate(picks):
+        check_close(merged_out[b], rl[i] if merged_lse is None else merged_lse[:, b], ro[i], rl[i],
+                    f"cfg4 request {b} merged output")
+    return {"status": "ok", "requests": picks, "max_abs": worst,
+            "against": "torch fp32 on the same cache bytes"}
 
 
 # ------------------------------------------------- config 2 / config 3 (N=1)
@@ -359,23 +490,37 @@ def rested(measure, pause=2.0):
     return result
 
 
-def time_loop(fn, steps, warmup):
+def time_loop(fn, steps, warmup, min_seconds=0.0):
+    """Device time per call of ``fn`` over ``steps`` calls after ``warmup``
+    (CUDA events on the current stream). With ``min_seconds`` the step count is
+    raised so that the timed region lasts at least that long (estimated from
+    three calls), which gives the clock sampler several samples; returns
+    (ms, steps) then, else ms."""
     import torch
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if min_seconds > 0:
+        s.record(stream)
+        for _ in range(3):
+            fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        est = max(s.elapsed_time(e) / 3, 1e-3)
+        steps = max(steps, int(min_seconds * 1e3 / est) + 1)
     s.record(stream)
     for _ in range(steps):
         fn()
     e.record(stream)
     torch.cuda.synchronize()
-    return s.elapsed_time(e) / steps
+    ms = s.elapsed_time(e) / steps
+    return (ms, steps) if min_seconds > 0 else ms
 
 
 def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False,
-                kv_slice=None, alibi=False):
+                kv_slice=None, alibi=False, min_seconds=0.0):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
 
     ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
@@ -410,69 +555,65 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
         k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
         kd = torch.full((len(lens), cfg["hkv"]), 0.5, device=dev)
         vd = torch.full((len(lens), cfg["hkv"]), 2.0, device=dev)
-        ms = time_loop(lambda: vllm_varlen(q, k, v, max(lens), cu, max(lens), cu_seqlens_k=cu, causal=True,
-                                           k_descale=kd, v_descale=vd, out=out), steps, warmup)
+        timed = time_loop(lambda: vllm_varlen(q, k, v, max(lens), cu, max(lens), cu_seqlens_k=cu, causal=True,
+                                              k_descale=kd, v_descale=vd, out=out), steps, warmup, min_seconds)
     else:
         slopes = (torch.tensor([2.0 ** (-8.0 * (h + 1) / cfg["hq"]) for h in range(cfg["hq"])], device=dev)
                   if alibi else None)
-        ms = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
-                                                      softcap=softcap, window_size=window, alibi_slopes=slopes,
-                                                      out=out),
-                       steps, warmup)
+        timed = time_loop(lambda: flash_attn_varlen_func(q, k, v, cu, cu, max(lens), max(lens), causal=True,
+                                                         softcap=softcap, window_size=window, alibi_slopes=slopes,
+                                                         out=out),
+                          steps, warmup, min_seconds)
+    ms, steps = timed if isinstance(timed, tuple) else (timed, steps)
     flops = cfg2_flops(lens, cfg, window[0])
     tflops = flops / (ms * 1e-3) / 1e12
-    return {"workload": "cfg2: varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
+    return {"workload": "cfg2 varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
                         + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else "")
-                        + (", FP8 E4M3 K/V with descales (16-bit copy + tcgen05 prefill)" if fp8_kv else "")
+                        + (", FP8 E4M3 K/V + descales" if fp8_kv else "")
                         + (f", KV heads {kv_slice[0]}..{kv_slice[1] - 1} only" if kv_slice else "")
                         + (", ALiBi slopes" if alibi else "")
                         + (" (small profiling case)" if small else ""),
-            "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "TFLOP/s": tflops,
+            "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "steps": steps,
+            "TFLOP/s": tflops,
             "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
-                         "peak_kind": f"{peak_kind} (bf16_tflops, burst)",
+                         "peak_kind": f"{peak_kind} bf16_tflops burst",
                          "frac_of_sustained": tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
 
 
-def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False):
-    """Config 3: paged bf16 decode, B=256, ctx ~U[512, 32768], page 16."""
-    import numpy as np
+def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False, min_seconds=0.0):
+    """Config 3: paged bf16 decode, B=256, ctx ~U[512, 32768], page 16, plus a
+    sampled check of the timed output against a torch fp32 reference."""
     import torch
     from flash_attn_b200._attention import attention
     cfg = dict(CFG3)
     if small:
         cfg["batch"] = 16  # profiling case
-    rng = np.random.default_rng(cfg["seed"])
-    ctx = rng.integers(cfg["cmin"], cfg["cmax"] + 1, size=cfg["batch"])
-    P = cfg["page"]
-    pages_per = (ctx + P - 1) // P
-    n_pages = int(pages_per.sum())
-    max_pages = int(pages_per.max())
-    perm = torch.from_numpy(rng.permutation(n_pages).astype(np.int32))
-    table = torch.zeros(cfg["batch"], max_pages, dtype=torch.int32)
-    off = 0
-    for b in range(cfg["batch"]):
-        table[b, :pages_per[b]] = perm[off:off + pages_per[b]]
-        off += pages_per[b]
-    dev = torch.device("cuda")
-    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
-    kc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
-    vc = torch.randn(n_pages, P, cfg["hkv"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
-    q = torch.randn(cfg["batch"], cfg["hq"], cfg["d"], device=dev, generator=g, dtype=torch.bfloat16)
-    table = table.to(dev)
-    used = torch.from_numpy(ctx.astype(np.int32)).to(dev)
-    cuq = torch.arange(cfg["batch"] + 1, dtype=torch.int32, device=dev)
-    out = torch.empty_like(q)
-    ms = time_loop(lambda: attention(q, kc, vc, cu_seqlens_q=cuq, seqused_k=used, max_seqlen_q=1,
-                                     max_seqlen_k=int(ctx.max()), block_table=table, out=out),
-                   steps, warmup)
-    nbytes = int(ctx.sum()) * cfg["hkv"] * 2 * cfg["d"] * 2 + int(pages_per.sum()) * 4 + 2 * q.numel() * 2
+    w = build_cfg3(cfg)
+    ctx, pages_per = w["ctx"], w["pages_per"]
+    out = torch.empty_like(w["q"])
+    lse_box = []
+
+    def call():
+        lse_box[:] = [attention(w["q"], w["k_cache"], w["v_cache"], cu_seqlens_q=w["cu_q"], seqused_k=w["used"],
+                                max_seqlen_q=1, max_seqlen_k=int(ctx.max()), block_table=w["table"], out=out)[1]]
+
+    timed = time_loop(call, steps, warmup, min_seconds=min_seconds)
+    ms, steps = timed if isinstance(timed, tuple) else (timed, steps)
+    worst = 0.0
+    picks = sample_requests(ctx)
+    for b in picks:
+        ro, rl = torch_decode_reference(w["q"][b], gather_request(w["k_cache"], w["table"], b, int(ctx[b]), cfg["page"]),
+                                        gather_request(w["v_cache"], w["table"], b, int(ctx[b]), cfg["page"]))
+        worst = max(worst, check_close(out[b], lse_box[0][:, b], ro, rl, f"cfg3 request {b}")[0])
+    nbytes = int(ctx.sum()) * cfg["hkv"] * 2 * cfg["d"] * 2 + int(pages_per.sum()) * 4 + 2 * w["q"].numel() * 2
     gbs = nbytes / (ms * 1e-3) / 1e9
-    del kc, vc
-    return {"workload": "cfg3: paged bf16 decode, B=256, ctx~U[512,32768], page 16, 32q/8kv, D=128",
-            "bytes_per_step": nbytes, "ms_per_step": ms, "TB/s": gbs / 1e3,
+    del w
+    return {"workload": "cfg3 paged bf16 decode, B=256, ctx~U[512,32768], page 16, 32q/8kv, D=128",
+            "bytes_per_step": nbytes, "ms_per_step": ms, "steps": steps, "TB/s": gbs / 1e3,
+            "parity": {"status": "ok", "requests": len(picks), "max_abs": worst},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} (hbm_gbs)"}}
+                         "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} hbm_gbs"}}
 
 
 # ------------------------------------------------------- config 5 (N=1)
@@ -677,14 +818,38 @@ def cpu_fp8_decode_sample(cfg, requests=1, seed=4):
     oracle.attention(q, k, v, cu_q, cu_k=cu_k, k_descale=desc, v_descale=desc)
     dt = time.perf_counter() - t0
     nbytes = requests * C * HK * 2 * D
-    return nbytes / dt / 1e12, dt, f"{requests} request(s) x {C} tokens of config 4 (FP8 decode + float64 attention)"
+    return nbytes / dt / 1e12, dt, f"{requests} request x {C} tokens of cfg4 (FP8 decode + float64 attention)"
+
+
+def blas_threads():
+    """Threads numpy's BLAS uses for the oracle's matrix products (the oracle's
+    element-wise numpy work runs on one thread)."""
+    try:
+        import threadpoolctl
+        counts = [d["num_threads"] for d in threadpoolctl.threadpool_info() if d.get("user_api") == "blas"]
+        if counts:
+            return max(counts)
+    except Exception:
+        pass
+    return os.cpu_count()
 
 
 def cpu_baseline_block(cfg):
     import numpy as np  # noqa: F401
     value, dt, sample = cpu_fp8_decode_sample(cfg)
-    return {"value": value, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": sample, "seconds": dt}
+    return {"value": value, "unit": "TB/s", "cores": blas_threads(), "host_cpus": os.cpu_count(),
+            "kind": "port", "sample": sample, "seconds": round(dt, 3)}
+
+
+def rounded(x, digits=6):
+    """Floats rounded to ``digits`` significant digits, recursively (short lines)."""
+    if isinstance(x, float):
+        return float(f"{x:.{digits}g}")
+    if isinstance(x, dict):
+        return {k: rounded(v, digits) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [rounded(v, digits) for v in x]
+    return x
 
 
 def run_reference(args):
@@ -710,10 +875,43 @@ def run_reference(args):
         "config": {"workload": "cfg4: long-context FP8 E4M3 paged decode (bounded CPU sample per step)",
                    "batch": cfg["batch"], "context": cfg["ctx"], "q_heads": cfg["hq"],
                    "kv_heads": cfg["hkv"], "head_dim": cfg["d"]},
-        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": blas_threads(), "host_cpus": os.cpu_count(),
+                         "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def check_build_id():
+    """The loaded library's build id; refuses to measure a library built from
+    other sources than the ones checked out beside this file."""
+    from flash_attn_b200 import _capi
+    sys.path.insert(0, os.path.join(ROOT, "flash-attn-mps_b200"))
+    import build
+    have, want = _capi.build_id(), build.source_hash()
+    if have != want:
+        raise SystemExit(f"libflash_attn_b200.so was built from other sources (build id {have}, sources {want}); "
+                         "run `python flash-attn-mps_b200/build.py`")
+    return have
+
+
+def secondary_line(name, r):
+    """One short JSON line for a secondary measurement."""
+    roof = r.get("roofline", {})
+    if "TFLOP/s" in r:
+        value, unit = r["TFLOP/s"], "TFLOP/s"
+    elif "TB/s" in r:
+        value, unit = r["TB/s"], "TB/s"
+    else:
+        value, unit = r["value"], r["unit"]
+    line = {"secondary": name, "value": round(value, 2), "unit": unit,
+            "ms_per_step": round(r["ms_per_step"], 4), "steps": r.get("steps"),
+            "roofline": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in roof.items()
+                         if k in ("bound", "achieved", "peak", "unit", "frac", "peak_kind")},
+            "clocks": r.get("clocks"), "workload": r.get("workload")}
+    for key in ("parity", "attention", "e2e"):
+        if key in r:
+            line[key] = r[key]
+    return line
 
 
 def main():
@@ -779,6 +977,7 @@ def main():
                               "data": "synthetic (seeded)",
                               "config": {"workload": r["workload"]}, "roofline": r["roofline"]}))
         return
+    build_id = check_build_id()
     res = run_fp8_decode(args, rank, world, peaks, peak_kind)
     multi = (multi_gpu_secondary(rank, world, peaks, peak_kind)
              if world > 1 and not args.no_secondary and not args.small else None)
@@ -788,20 +987,27 @@ def main():
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"],
                 "e2e": res["e2e"], "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
-                "clocks": res["clocks"]}
+                "clocks": res["clocks"], "parity": res["parity"], "build_id": build_id}
+        # Secondary workloads: one short JSON line each, printed before the
+        # headline line (the last line), the most important one last.
         if world == 1 and not args.no_secondary and not args.small:
-            line["secondary"] = {
-                "prefill_cfg2": rested(lambda: run_prefill(peaks, peak_kind)),
-                "prefill_cfg2_softcap_window": rested(lambda: run_prefill(peaks, peak_kind, softcap=50.0,
-                                                                          window=(1024, 0))),
-                "prefill_cfg2_fp8kv": rested(lambda: run_prefill(peaks, peak_kind, steps=10, warmup=3, fp8_kv=True)),
-                "decode_cfg3": rested(lambda: run_bf16_decode(peaks, peak_kind)),
-                "serving_cfg5": run_serving(peaks, peak_kind)}
+            secondaries = [
+                ("serving_cfg5", lambda: run_serving(peaks, peak_kind)),
+                ("decode_cfg3", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=1.2))),
+                ("prefill_cfg2_fp8kv", lambda: rested(lambda: run_prefill(peaks, peak_kind, fp8_kv=True,
+                                                                          min_seconds=1.2))),
+                ("prefill_cfg2_softcap_window", lambda: rested(lambda: run_prefill(
+                    peaks, peak_kind, softcap=50.0, window=(1024, 0), min_seconds=1.2))),
+                ("prefill_cfg2", lambda: rested(lambda: run_prefill(peaks, peak_kind, min_seconds=1.2))),
+            ]
+            for name, measure in secondaries:
+                print(json.dumps(rounded(secondary_line(name, measure()))), flush=True)
         if multi:
-            line["secondary"] = multi
+            for name, r in multi.items():
+                print(json.dumps(rounded(dict({"secondary": name}, **r))), flush=True)
         if world == 1 and not args.no_cpu_baseline and not args.small:
             line["cpu_baseline"] = cpu_baseline_block(CFG4)
-        print(json.dumps(line))
+        print(json.dumps(rounded(line)))
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -1,14 +1,14 @@
 // Attention dispatch (host side of the C ABI): argument checks, kernel choice,
 // split-KV planning and the partial merge.
 //
-// Routing follows the reference dispatcher (flash_attn_mps/_attention.py:170-320):
+// Routing follows the reference dispatcher (flash_attn_mps/_attention.py:88-238):
 //   * one query per request, not deterministic, no ALiBi, no mask
-//     -> decode (_attention.py:216-229 -> _decode.py:40-99): the tensor-core
+//     -> decode (_attention.py:134-147 -> _decode.py:40-99): the tensor-core
 //        decode kernel when its envelope fits, else the generic kernel;
 //   * eligible dense/varlen prefill -> the tcgen05 kernel (the reference's
-//     "fast" predicate, _attention.py:231-240);
+//     "fast" predicate, _attention.py:149-158);
 //   * everything else -> the generic kernel with the reference's split rule
-//     (_attention.py:241-243).
+//     (_attention.py:159-161).
 // The choice depends on shapes, dtypes, strides and flags only, never on
 // tensor values or lengths beyond the caller's max_seqlen_*.
 #include <cudaTypedefs.h>
@@ -242,7 +242,18 @@ void fill_params(const fa_attention_args* a, AttnParams* p) {
   p->splits = 1;
 }
 
-int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
+// Bytes of split partials (outputs, then LSEs) for `splits` splits.
+size_t split_part_bytes(const AttnParams& p, int splits) {
+  return ((size_t)splits * p.T * p.HQ * p.DV * sizeof(float) + 255) / 256 * 256;
+}
+size_t split_lse_bytes(const AttnParams& p, int splits) {
+  return ((size_t)splits * p.HQ * p.T * sizeof(float) + 255) / 256 * 256;
+}
+
+// part_cap > 0: when the library chooses a decode split count
+// (num_splits == 0), lower it until the split partials fit in part_cap bytes
+// (down to one split, which writes the outputs directly and needs none).
+int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan, size_t part_cap = 0) {
   *plan = Plan{kRouteGeneric, 1, 0, 0, 0};
   // Batch-invariant mode (deterministic, or num_splits == 1 as vLLM's
   // batch-invariant path passes it): the kernel choice depends on dtypes and
@@ -272,6 +283,12 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
     } else {
       // _decode.py:63-64
       plan->splits = a->num_splits > 0 ? a->num_splits : std::max(1, std::min(32, (eff + 255) / 256));
+    }
+    if (part_cap > 0 && a->num_splits == 0) {
+      while (plan->splits > 1 &&
+             split_part_bytes(p, plan->splits) + split_lse_bytes(p, plan->splits) > part_cap)
+        --plan->splits;
+      if (plan->route == kRouteDecode) plan->span = std::max(1, (eff + plan->splits - 1) / plan->splits);
     }
   } else {
     AttnParams view;
@@ -304,8 +321,8 @@ int make_plan(const fa_attention_args* a, const AttnParams& p, Plan* plan) {
     if (mma_attention_supported(q)) plan->route = kRouteMma;
   }
   if (plan->splits > 1) {
-    plan->part_bytes = ((size_t)plan->splits * p.T * p.HQ * p.DV * sizeof(float) + 255) / 256 * 256;
-    plan->lse_bytes = ((size_t)plan->splits * p.HQ * p.T * sizeof(float) + 255) / 256 * 256;
+    plan->part_bytes = split_part_bytes(p, plan->splits);
+    plan->lse_bytes = split_lse_bytes(p, plan->splits);
   }
   return FA_OK;
 }
@@ -333,7 +350,9 @@ extern "C" int fa_pipeline_timeouts(int clear) {
   return (a ? 1 : 0) | (b ? 2 : 0);
 }
 
-extern "C" int fa_attention_workspace_size(const fa_attention_args* a, size_t* bytes) {
+namespace fab {
+
+int attention_workspace_capped(const fa_attention_args* a, size_t* bytes, size_t part_cap) {
   FAB_CHECK_ARG(bytes != nullptr, "bytes must not be null");
   *bytes = 0;
   int rc = validate(a);
@@ -342,20 +361,20 @@ extern "C" int fa_attention_workspace_size(const fa_attention_args* a, size_t* b
   AttnParams p;
   fill_params(a, &p);
   Plan plan;
-  rc = make_plan(a, p, &plan);
+  rc = make_plan(a, p, &plan, part_cap);
   if (rc) return rc;
   *bytes = plan.part_bytes + plan.lse_bytes;
   return FA_OK;
 }
 
-extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
+int attention_fwd_capped(const fa_attention_args* a, void* stream, size_t part_cap) {
   int rc = validate(a);
   if (rc) return rc;
   if (a->q.shape[0] == 0) return FA_OK;
   AttnParams p;
   fill_params(a, &p);
   Plan plan;
-  rc = make_plan(a, p, &plan);
+  rc = make_plan(a, p, &plan, part_cap);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (plan.route == kRoutePrefill || plan.route == kRouteFp8Prefill) {
@@ -415,4 +434,14 @@ extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
     rc = launch_merge_partials(m, st);
   }
   return rc;
+}
+
+}  // namespace fab
+
+extern "C" int fa_attention_workspace_size(const fa_attention_args* a, size_t* bytes) {
+  return fab::attention_workspace_capped(a, bytes, 0);
+}
+
+extern "C" int fa_attention_fwd(const fa_attention_args* a, void* stream) {
+  return fab::attention_fwd_capped(a, stream, 0);
 }

@@ -2,9 +2,9 @@
 // quantisation), append_kvcache and rotary position embedding.
 //
 // Semantics follow the reference flash_attn_mps 0.1.0:
-//   store   kernels/cache.metal:20-39, host _cache.py:166-184
-//   append  kernels/cache.metal:41-56, host _cache.py:198-226
-//   rotate  kernels/cache.metal:58-76, host _cache.py:229-254
+//   store   kernels/cache.metal:20-39, host _cache.py:67-85
+//   append  kernels/cache.metal:41-56, host _cache.py:99-127
+//   rotate  kernels/cache.metal:58-76, host _cache.py:130-155
 // store_kvcache: a CTA row of threads covers the (head, 16-byte chunk) pairs of
 // one token, CTA rows take successive tokens (grid-stride over tokens), so the
 // slot lookup and page split happen once per token and a thread's head (and

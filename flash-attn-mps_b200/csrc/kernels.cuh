@@ -23,7 +23,7 @@ int encode_tensor_map(void* map, int dtype, int rank, const void* ptr, const uin
 
 // Flattened attention parameters: device pointers, element strides and
 // feature flags. Mirrors the reference's parameter vector
-// (flash_attn_mps/_attention.py:10-16 _META, filled at 265-295).
+// (flash_attn_mps/_attention.py:10-16 _META, filled at 183-213).
 struct AttnParams {
   const void* q; const void* k; const void* v;
   int32_t qt, kt, vt;              // element dtypes (FA_*)
@@ -82,6 +82,11 @@ int64_t fp8_prefill_rows(const AttnParams& p);
 bool fp8_prefill_view(const AttnParams& p, AttnParams* view);
 int launch_kv_dequant(const AttnParams& p, void* k_out, void* v_out, int32_t* cu_out, int32_t* used_out,
                       cudaStream_t stream);
+// fa_attention_workspace_size / fa_attention_fwd with a bound on the split
+// partials: part_cap > 0 lowers a library-chosen decode split count until its
+// partials fit in part_cap bytes (0 = no bound, the public behaviour).
+int attention_workspace_capped(const fa_attention_args* a, size_t* bytes, size_t part_cap);
+int attention_fwd_capped(const fa_attention_args* a, void* stream, size_t part_cap);
 // Timed-out pipeline waits recorded by the prefill / TMA decode kernels on the
 // current device (1 = some wait gave up, 0 = none, -1 = CUDA error).
 int prefill_timeout_flag(bool clear);

@@ -29,7 +29,7 @@
 // Semantics (lower-right causal, natural-log LSE, zero output and -inf LSE
 // for rows with no visible key) follow the reference's fast kernel
 // flash_attn_mps/kernels/attention_fast.metal:94-597 and its eligibility
-// predicate flash_attn_mps/_attention.py:231-240.
+// predicate flash_attn_mps/_attention.py:149-158.
 #include <algorithm>
 #include <type_traits>
 #include <mutex>

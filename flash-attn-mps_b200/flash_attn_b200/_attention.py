@@ -1,7 +1,7 @@
 """Attention entry over the CUDA library (mirrors flash_attn_mps/_attention.py).
 
 ``attention`` keeps the reference signature and checks
-(``flash_attn_mps/_attention.py:170-215``) and returns ``(out, lse)`` with the
+(``flash_attn_mps/_attention.py:88-161``) and returns ``(out, lse)`` with the
 natural-log LSE in ``[heads, total_q]`` order. Kernel choice, split-KV and the
 partial merge happen inside ``fa_attention_fwd``; this module only validates,
 allocates the caller-visible outputs and the split workspace, and passes

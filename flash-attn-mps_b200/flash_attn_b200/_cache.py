@@ -1,11 +1,11 @@
 """KV-cache writes over the CUDA library (mirrors flash_attn_mps/_cache.py).
 
-* ``store_kvcache`` (reference ``_cache.py:166-184``): slot scatter of new K/V
+* ``store_kvcache`` (reference ``_cache.py:67-85``): slot scatter of new K/V
   rows, bit-exact copies or saturating FP8 E4M3 codes of ``x / scale[h]``;
   K and V go out in one launch.
-* ``append_kvcache`` (``_cache.py:198-226``): append at the old lengths of a
+* ``append_kvcache`` (``_cache.py:99-127``): append at the old lengths of a
   continuous or paged cache; lengths are not modified.
-* ``rotary`` (``_cache.py:229-254``): RoPE of Q and new K at their absolute
+* ``rotary`` (``_cache.py:130-155``): RoPE of Q and new K at their absolute
   positions, interleaved or split-half.
 """
 

@@ -60,11 +60,13 @@ class AttentionArgs(ctypes.Structure):
 
 _P = ctypes.POINTER
 # (name, argtypes) of every exported entry point; tests check the header too.
-_RESTYPES = {"fa_last_error": ctypes.c_char_p, "fa_kernel_launches": ctypes.c_uint64}
+_RESTYPES = {"fa_last_error": ctypes.c_char_p, "fa_build_id": ctypes.c_char_p,
+             "fa_kernel_launches": ctypes.c_uint64}
 
 SIGNATURES = {
     "fa_abi_version": [],
     "fa_last_error": [],
+    "fa_build_id": [],
     "fa_pipeline_timeouts": [ctypes.c_int],
     "fa_kernel_launches": [],
     "fa_attention_workspace_size": [_P(AttentionArgs), _P(ctypes.c_size_t)],
@@ -99,6 +101,11 @@ def library():
                     fn.restype = _RESTYPES.get(name, ctypes.c_int)
                 _lib = lib
     return _lib
+
+
+def build_id():
+    """Hash of the sources the loaded library was built from (build.py source_hash)."""
+    return library().fa_build_id().decode()
 
 
 def kernel_launches():

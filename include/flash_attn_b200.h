@@ -63,7 +63,7 @@ typedef struct fa_tensor {
 
 /*
  * Arguments of one attention call. Field meanings follow the reference's
- * internal attention() (flash_attn_mps/_attention.py:170-176):
+ * internal attention() (flash_attn_mps/_attention.py:88-94):
  *   q [Tq,Hq,Dq]; k/v packed [Tk,Hkv,Dq|Dv] or paged [N,P,Hkv,Dq|Dv];
  *   out [Tq,Hq,Dv] (f16/bf16/f32, any strides); lse [Hq,Tq] f32.
  * Query row i of a request with Sq queries and Sk keys sits at absolute
@@ -113,6 +113,15 @@ int fa_abi_version(void);
 const char* fa_last_error(void);
 
 /*
+ * Build identity: 16 hex digits hashing every compiled source file, header and
+ * compiler flag the library was built from (flash-attn-mps_b200/build.py,
+ * source_hash), so a caller can check that a prebuilt library matches the
+ * sources it ships with. No counterpart in the reference, which compiles its
+ * Metal shaders from source at first use.
+ */
+const char* fa_build_id(void);
+
+/*
  * Pipeline wait time-outs on the current device since the last clear:
  * bit 0 = the tensor-core prefill kernel, bit 1 = the TMA paged-decode kernel.
  * Every mbarrier wait in those kernels gives up after a bounded number of
@@ -136,7 +145,7 @@ uint64_t fa_kernel_launches(void);
 /*
  * Bytes of device workspace fa_attention_fwd needs for these arguments
  * (split-KV partial outputs and LSEs). Host-only; reads no tensor values.
- * Replaces the partial-buffer allocation of flash_attn_mps/_attention.py:244-249
+ * Replaces the partial-buffer allocation of flash_attn_mps/_attention.py:162-167
  * and _decode.py:88-91.
  */
 int fa_attention_workspace_size(const fa_attention_args* args, size_t* bytes);
@@ -144,7 +153,7 @@ int fa_attention_workspace_size(const fa_attention_args* args, size_t* bytes);
 /*
  * Attention forward: dispatch (decode / tcgen05 prefill / generic), split-KV
  * and the LSE merge, writing out and lse.
- * Replaces flash_attn_mps/_attention.py:170-320 (attention) together with
+ * Replaces flash_attn_mps/_attention.py:88-238 (attention) together with
  * flash_attn_mps/_decode.py:40-99 (decode_attention) which it routes to.
  */
 int fa_attention_fwd(const fa_attention_args* args, void* stream);
@@ -157,10 +166,13 @@ int fa_attention_fwd(const fa_attention_args* args, void* stream);
  * ignored). For callers that cannot allocate device memory: FFI hosts holding
  * only raw pointers from another allocator, processes whose device memory is
  * pre-reserved by a pool they do not control, and decode loops that must not
- * call cudaMalloc. Requests whose partials exceed 32 MiB fail with
- * FA_ERR_INVALID before any launch. All calls on a device share the array:
- * calls whose GPU work overlaps race. The first call on a device resolves the
- * array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * call cudaMalloc. With num_splits == 0 the library's split count is lowered
+ * until the partials fit in 32 MiB; an explicit num_splits whose partials
+ * exceed 32 MiB fails with FA_ERR_INVALID before any launch. All calls on a
+ * device share the array: calls whose GPU work overlaps race. The first call
+ * on a device resolves the array's address (cudaGetSymbolAddress) and caches
+ * it with the current CUDA context (another context resolves it again); make
+ * that first call before any stream capture.
  * This entry point has no counterpart in the reference.
  */
 int fa_decode_fwd_noalloc(const fa_attention_args* args, void* stream);
@@ -171,7 +183,7 @@ int fa_decode_fwd_noalloc(const fa_attention_args* args, void* stream);
  * cache stores the saturating round-to-nearest-even code of x/scale[h]
  * (scale f32 scalar or [Hkv], absent = 1); other caches must match x's dtype
  * and receive a bit-exact copy. Either K or V side may be absent (ptr NULL).
- * Replaces flash_attn_mps/_cache.py:166-184 (store_kvcache) and its kernel
+ * Replaces flash_attn_mps/_cache.py:67-85 (store_kvcache) and its kernel
  * kernels/cache.metal:20-39.
  */
 int fa_store_kvcache(const fa_tensor* key, const fa_tensor* value,
@@ -185,7 +197,7 @@ int fa_store_kvcache(const fa_tensor* key, const fa_tensor* value,
  * cache [Bcache,capacity,Hkv,D] (row cache_batch_idx[b] when given) or of a
  * paged cache through block_table [B,pages]; out-of-range rows, positions and
  * pages are skipped; lengths are not modified.
- * Replaces flash_attn_mps/_cache.py:198-226 (append_kvcache), kernel
+ * Replaces flash_attn_mps/_cache.py:99-127 (append_kvcache), kernel
  * kernels/cache.metal:41-56.
  */
 int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
@@ -199,7 +211,7 @@ int fa_append_kvcache(const fa_tensor* key, const fa_tensor* value,
  * Rotary position embedding of x [B,S,H,D] into out (same shape and dtype):
  * position lengths[b] (+ j when advance), cos/sin f32 [positions, rot/2],
  * interleaved or split-half pairs, dims beyond rot copied.
- * Replaces flash_attn_mps/_cache.py:229-254 (rotary), kernel
+ * Replaces flash_attn_mps/_cache.py:130-155 (rotary), kernel
  * kernels/cache.metal:58-76.
  */
 int fa_rotary(const fa_tensor* x, const fa_tensor* out,
@@ -216,7 +228,7 @@ int fa_rotary(const fa_tensor* x, const fa_tensor* out,
  * advance_q) into q_out. cos/sin: [positions, rotary_dim/2] of any float
  * dtype. Results equal fa_rotary followed by fa_append_kvcache bit for bit.
  * No single counterpart in the reference: it fuses flash_attn_mps/_cache.py:
- * 229-254 (rotary, kernels/cache.metal:58-76) with _cache.py:198-226 (append,
+ * 130-155 (rotary, kernels/cache.metal:58-76) with _cache.py:99-127 (append,
  * kernels/cache.metal:41-56) as called from interface.py:231-307.
  */
 int fa_rotary_append_kvcache(const fa_tensor* q, const fa_tensor* q_out,

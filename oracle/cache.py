@@ -1,14 +1,14 @@
 """KV-cache writes restated in numpy (oracle; test infrastructure only).
 
 * ``store_kvcache`` follows ``flash_attn_mps/kernels/cache.metal:20-39`` and
-  ``_cache.py:166-184``: ``cache[slot // P, slot % P, h, :] = x[t, h, :]``,
+  ``_cache.py:67-85``: ``cache[slot // P, slot % P, h, :] = x[t, h, :]``,
   or the saturating E4M3 code of ``float32(x) / float32(scale[h])`` for an FP8
   cache; slots < 0 or >= N*P are skipped.
-* ``append_kvcache`` follows ``cache.metal:41-56`` and ``_cache.py:198-226``:
+* ``append_kvcache`` follows ``cache.metal:41-56`` and ``_cache.py:99-127``:
   new token j of request b goes to position ``lengths[b] + j`` of cache row
   ``cache_batch_idx[b]`` (continuous) or of page ``block_table[b, pos // P]``
   (paged); out-of-range rows, positions and pages are skipped.
-* ``rotary`` follows ``cache.metal:58-76`` and ``_cache.py:229-254``: RoPE at
+* ``rotary`` follows ``cache.metal:58-76`` and ``_cache.py:130-155``: RoPE at
   ``lengths[b] + j`` (Q advances with j only when causal or local), in
   interleaved or split-half pairing; dims beyond ``2 * rotary_dim/2`` copy.
 

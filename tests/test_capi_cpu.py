@@ -37,6 +37,14 @@ def test_library_exports_every_declared_symbol():
     assert _capi.kernel_launches() >= 0
 
 
+def test_library_build_id_matches_the_sources():
+    # The library is a build artefact that travels beside the sources; its
+    # embedded hash must describe exactly the sources checked out here.
+    import build
+    assert _capi.build_id() == build.source_hash(), (
+        "the shared library was built from other sources; run `python flash-attn-mps_b200/build.py`")
+
+
 def test_struct_layout_matches_header_order():
     # 19 tensor descriptors (80 bytes each), 13 4-byte scalars, then (ABI 2)
     # one more descriptor (8-byte aligned) and 2 scalars.

@@ -6,9 +6,14 @@ memory is pre-reserved by a pool it does not control, or a decode loop that
 must not call cudaMalloc. fa_decode_fwd_noalloc keeps the split-KV partials in
 a static device array inside the library. This test calls it through the C ABI
 twice in a row and checks each result against the existing entry point
-(fa_attention_fwd with a caller workspace), plus the clear rejection of a
-request whose partials exceed the static array. It lives in its own file,
-collected last, and passes alone in a fresh process or after the other tests.
+(fa_attention_fwd with a caller workspace). Both run the same plan and the
+same kernels, so their results must be bit-identical: a misplaced partial or
+LSE offset inside the static array would change them only slightly, and a
+tolerance could hide it. It also covers the num_splits == 1 (batch-invariant)
+route after a split call has left data in the array, a library-chosen split
+count lowered to fit the array, and the clear rejection of an explicit split
+count whose partials exceed it. It lives in its own file, collected last, and
+passes alone in a fresh process or after the other tests.
 """
 
 import ctypes
@@ -21,10 +26,10 @@ from flash_attn_b200 import _attention, _capi
 pytestmark = pytest.mark.gpu
 
 
-def _case(device, seed, kv_dtype):
+def _case(device, seed, kv_dtype, num_splits=8, lengths=(3000, 1, 2047, 1500)):
     g = torch.Generator().manual_seed(seed)
-    batch, hq, hk, d, page = 4, 16, 4, 128, 16
-    lengths = [3000, 1, 2047, 1500]
+    lengths = list(lengths)
+    batch, hq, hk, d, page = len(lengths), 16, 4, 128, 16
     columns = (max(lengths) + page - 1) // page
     pages = batch * columns + 3
     k = torch.randn(pages, page, hk, d, generator=g)
@@ -42,7 +47,7 @@ def _case(device, seed, kv_dtype):
               s_aux=None, q_descale=None,
               k_descale=torch.full((batch, hk), 1 / 40, device=device) if kv_dtype == torch.float8_e4m3fn else None,
               v_descale=torch.full((batch, hk), 1 / 40, device=device) if kv_dtype == torch.float8_e4m3fn else None,
-              num_splits=8, mask_mod=None, aux_tensors=None, leftpad_k=None, deterministic=False)
+              num_splits=num_splits, mask_mod=None, aux_tensors=None, leftpad_k=None, deterministic=False)
     return q.to(device), k.to(device), v.to(device), kw
 
 
@@ -61,15 +66,50 @@ def _existing(q, k, v, kw):
     return _attention.run(q, k, v, out, lse, **kw)
 
 
+def _assert_identical(got, got_lse, want, want_lse):
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), f"out differs, max-abs {(got.float() - want.float()).abs().max().item()}"
+    assert torch.equal(got_lse, want_lse), "lse differs"
+
+
 @pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
 def test_noalloc_decode_matches_existing_entry_point_twice(device, kv_dtype):
     for seed in (0, 1):  # two calls in a row share the static scratch
         q, k, v, kw = _case(device, seed, kv_dtype)
         want, want_lse = _existing(q, k, v, kw)
         got, got_lse = _noalloc(q, k, v, kw)
-        torch.cuda.synchronize()
-        torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=5e-2)
-        torch.testing.assert_close(got_lse, want_lse, atol=1e-3, rtol=0)
+        _assert_identical(got, got_lse, want, want_lse)
+
+
+@pytest.mark.parametrize("kv_dtype", [torch.bfloat16, torch.float8_e4m3fn])
+def test_noalloc_single_split_after_a_split_call(device, kv_dtype):
+    # A split call first leaves partials in the static array; num_splits == 1
+    # then runs the batch-invariant route, whose work counter lives in the
+    # same array and must be cleared by that launch, twice in a row.
+    q, k, v, kw = _case(device, 3, kv_dtype, num_splits=8)
+    _noalloc(q, k, v, kw)
+    for seed in (4, 5):
+        q, k, v, kw = _case(device, seed, kv_dtype, num_splits=1)
+        want, want_lse = _existing(q, k, v, kw)
+        got, got_lse = _noalloc(q, k, v, kw)
+        _assert_identical(got, got_lse, want, want_lse)
+
+
+def test_noalloc_lowers_a_library_chosen_split_count_to_fit(device):
+    # 512 requests x 32 query heads: the library's own rule picks 4 splits for
+    # FP8 K/V, whose partials (32 MiB + LSEs) exceed the static array; with
+    # num_splits == 0 the entry point lowers the count to 3 instead of failing.
+    lengths = [1024] * 512
+    q, k, v, kw = _case(device, 6, torch.float8_e4m3fn, num_splits=0, lengths=lengths)
+    q = q.repeat(1, 2, 1)  # 32 query heads over 4 KV heads
+    want, want_lse = _existing(q, k, v, dict(kw, num_splits=3))
+    for _ in range(2):
+        got, got_lse = _noalloc(q, k, v, kw)
+        _assert_identical(got, got_lse, want, want_lse)
+    default, default_lse = _existing(q, k, v, kw)  # 4 splits, caller workspace
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got.float(), default.float(), atol=2e-2, rtol=5e-2)
+    torch.testing.assert_close(got_lse, default_lse, atol=1e-3, rtol=0)
 
 
 def test_noalloc_rejects_partials_beyond_the_static_scratch(device):
