@@ -49,18 +49,64 @@ def load_peaks():
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+    """SM clocks and throttle reasons sampled while a measurement runs
+    (read-only). In-process NVML reads every 20 ms, so that timed regions of
+    tens of milliseconds still get several samples; `nvidia-smi -lms 200` when
+    NVML is unavailable. The device is the torch device `index`, matched to
+    NVML by PCI bus id."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): HW slowdown 0x8 (and HW power
+    # brake 0x80), HW thermal 0x40, SW thermal 0x20, SW power cap 0x4.
+    REASONS = (("hw_slowdown", 0x8 | 0x80), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, index):
+    def __init__(self, index, period_s=0.02):
         self.index = index
+        self.period = period_s
         self.proc = None
+        self.thread = None
         self.lines = []
+        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.smax = None
+        self.stop_flag = threading.Event()
+        self.source = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def start(self):
+        try:
+            import pynvml
+            handle = self._nvml_handle()
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                        self.samples.append((float(sm), int(rs)))
+                    except Exception:
+                        pass
+                    self.stop_flag.wait(self.period)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml 20 ms"
+            return
+        except Exception:
+            self.thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -68,6 +114,7 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            self.source = "nvidia-smi 200 ms"
         except OSError:
             self.proc = None
 
@@ -76,8 +123,15 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.source is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            sm = [x for x, _ in self.samples]
+            reasons = sorted({name for _, mask in self.samples for name, bit in self.REASONS if mask & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                    "reasons": reasons, "samples": len(sm), "source": self.source}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -85,7 +139,7 @@ class ClockSampler:
             self.proc.kill()
         self.thread.join(timeout=2)
         sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [n for n, _ in self.REASONS]
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
@@ -99,7 +153,7 @@ class ClockSampler:
                 if flag.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": self.source}
 
 
 # ------------------------------------------------------------------ helpers
@@ -520,7 +574,7 @@ def time_loop(fn, steps, warmup, min_seconds=0.0):
 
 
 def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False,
-                kv_slice=None, alibi=False, min_seconds=0.0):
+                kv_slice=None, alibi=False, min_seconds=0.0, sustained=False):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
 
     ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
@@ -575,10 +629,19 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
                         + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "steps": steps,
             "TFLOP/s": tflops,
-            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"],
-                         "peak_kind": f"{peak_kind} bf16_tflops burst",
-                         "frac_of_sustained": tflops / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])}}
+            "roofline": roofline_tensor(tflops, peaks, peak_kind, sustained)}
+
+
+def roofline_tensor(tflops, peaks, peak_kind, sustained=False):
+    """Tensor-bound roofline: the burst cuBLAS bf16 peak for a kernel timed in a
+    short window at full clocks, the sustained one (seconds-long loop under the
+    power cap) for a window long enough to reach the power cap."""
+    burst = peaks["bf16_tflops"]
+    sus = peaks.get("bf16_tflops_sustained", burst)
+    peak = sus if sustained else burst
+    return {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s", "frac": tflops / peak,
+            "peak_kind": f"{peak_kind} bf16_tflops{'_sustained' if sustained else ' burst'}",
+            "frac_of_burst": tflops / burst, "frac_of_sustained": tflops / sus}
 
 
 def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False, min_seconds=0.0):
@@ -657,6 +720,51 @@ def cpu_serving_sample(prompt=256, decode_steps=16, seed=5):
             "kind": "port", "seconds": dt,
             "sample": f"1 request: {prompt}-token prompt + {decode_steps} greedy decode steps, full 28-layer "
                       f"model, torch CPU GEMMs + float64 SDPA attention (the reference's frozen SDPA path)"}
+
+
+def run_store(peaks, peak_kind, steps=20, warmup=3, fp8=True, tokens=524288, min_seconds=0.0):
+    """store_kvcache bandwidth on config 4's cache-build shape: `tokens` new
+    bf16 K and V rows [T, 8, 128] scattered into a page-16 cache through a
+    seeded permutation of slots, quantised to FP8 E4M3 with per-head scales
+    U[1/448, 4/448] (or copied as bf16). Algorithmic bytes per call: inputs read
+    + cache written + slots. Checks a sample of the written codes against
+    torch's float8_e4m3fn cast of clamp(x / scale) (or the bf16 bits)."""
+    import torch
+    from flash_attn_b200 import store_kvcache
+    dev = torch.device("cuda")
+    H, D, P = 8, 128, 16
+    gen = torch.Generator(device="cpu").manual_seed(11)
+    slots = torch.randperm(tokens, generator=gen).to(torch.int64).to(dev)
+    ks = ((1 + 3 * torch.rand(H, generator=gen)) / 448).to(dev)
+    vs = ((1 + 3 * torch.rand(H, generator=gen)) / 448).to(dev)
+    g = torch.Generator(device=dev).manual_seed(12)
+    k = torch.randn(tokens, H, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(tokens, H, D, device=dev, generator=g).to(torch.bfloat16)
+    cdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc = torch.empty(tokens // P, P, H, D, dtype=cdt, device=dev)
+    vc = torch.empty_like(kc)
+    sc = dict(k_scale=ks, v_scale=vs) if fp8 else {}
+    timed = time_loop(lambda: store_kvcache(k, v, kc, vc, slots, **sc), steps, warmup, min_seconds)
+    ms, steps = timed if isinstance(timed, tuple) else (timed, steps)
+    # Sampled check: the rows of 4096 seeded tokens.
+    pick = torch.randperm(tokens, generator=gen)[:4096].to(dev)
+    sl = slots[pick]
+    for x, cache, scale in ((k, kc, ks), (v, vc, vs)):
+        got = cache.view(-1, H, D)[sl]
+        want = ((x[pick].float() / scale.reshape(1, -1, 1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+                if fp8 else x[pick])
+        if not torch.equal(got.view(torch.uint8), want.view(torch.uint8)):
+            raise AssertionError("store_kvcache wrote other bytes than the reference cast")
+    elems = 2 * tokens * H * D
+    nbytes = elems * (2 + (1 if fp8 else 2)) + tokens * 8
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    del k, v, kc, vc
+    return {"workload": f"store_kvcache bf16 -> {'FP8 E4M3 (per-head scales)' if fp8 else 'bf16'}, "
+                        f"{tokens} tokens x 8 heads x 128 (K and V), random slots, page 16",
+            "bytes_per_step": nbytes, "ms_per_step": ms, "steps": steps, "TB/s": gbs / 1e3,
+            "parity": {"status": "ok", "against": "torch cast of clamp(x / scale) (bit-exact), 4096 rows"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} hbm_gbs"}}
 
 
 def run_serving(peaks, peak_kind, steps=2, warmup=3, small=False, path="fused", cpu_baseline=False):
@@ -906,7 +1014,7 @@ def secondary_line(name, r):
     line = {"secondary": name, "value": round(value, 2), "unit": unit,
             "ms_per_step": round(r["ms_per_step"], 4), "steps": r.get("steps"),
             "roofline": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in roof.items()
-                         if k in ("bound", "achieved", "peak", "unit", "frac", "peak_kind")},
+                         if k in ("bound", "achieved", "peak", "unit", "frac", "peak_kind", "frac_of_burst")},
             "clocks": r.get("clocks"), "workload": r.get("workload")}
     for key in ("parity", "attention", "e2e"):
         if key in r:
@@ -921,7 +1029,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
-                                           "prefill_alibi", "bf16_decode", "serving"],
+                                           "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -963,6 +1071,10 @@ def main():
             elif args.workload == "prefill_fp8kv":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)
                 value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload in ("store_fp8", "store_bf16"):
+                r = run_store(peaks, peak_kind, steps=args.steps, warmup=args.warmup,
+                              fp8=args.workload == "store_fp8", tokens=65536 if args.small else 524288)
+                value, unit = r["TB/s"], "TB/s"
             elif args.workload == "prefill_softcap_window":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, softcap=50.0,
                                 window=(1024, 0), small=args.small)
@@ -993,12 +1105,17 @@ def main():
         if world == 1 and not args.no_secondary and not args.small:
             secondaries = [
                 ("serving_cfg5", lambda: run_serving(peaks, peak_kind)),
+                ("store_kvcache_fp8", lambda: rested(lambda: run_store(peaks, peak_kind, min_seconds=1.0), 0.5)),
                 ("decode_cfg3", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=1.2))),
                 ("prefill_cfg2_fp8kv", lambda: rested(lambda: run_prefill(peaks, peak_kind, fp8_kv=True,
-                                                                          min_seconds=1.2))),
+                                                                          min_seconds=0.15))),
                 ("prefill_cfg2_softcap_window", lambda: rested(lambda: run_prefill(
-                    peaks, peak_kind, softcap=50.0, window=(1024, 0), min_seconds=1.2))),
-                ("prefill_cfg2", lambda: rested(lambda: run_prefill(peaks, peak_kind, min_seconds=1.2))),
+                    peaks, peak_kind, softcap=50.0, window=(1024, 0), min_seconds=0.15))),
+                # Over a window of seconds the GPU reaches its power cap and
+                # lowers its clocks: that run is held against the sustained peak.
+                ("prefill_cfg2_sustained", lambda: rested(lambda: run_prefill(peaks, peak_kind, min_seconds=2.0,
+                                                                              sustained=True))),
+                ("prefill_cfg2", lambda: rested(lambda: run_prefill(peaks, peak_kind, min_seconds=0.15))),
             ]
             for name, measure in secondaries:
                 print(json.dumps(rounded(secondary_line(name, measure()))), flush=True)

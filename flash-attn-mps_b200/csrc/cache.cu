@@ -184,6 +184,161 @@ __global__ void __launch_bounds__(256) store_kernel(StoreArgs a) {
   }
 }
 
+// ---- warp-per-token-row store (16-bit inputs, unit inner strides)
+//
+// One warp owns one token row (H heads x D dims) at a time; lane L handles
+// the 16-byte input vectors L, L+32, ... (NV per lane), whose head, source
+// and destination offsets and FP8 scale constants are fixed for the whole
+// launch and computed once. The source rows do not depend on the slots, so a
+// warp issues the data loads of kRowU tokens together with their slot loads
+// (one broadcast load per token) and only the stores wait on the slots.
+// E4M3 quantisation per pair of elements: q = RN(x y) clamped to +-1e4,
+// r = x - q s and RN(q + r y) (Markstein's correctly rounded quotient,
+// y = RN(1/s)) with the products and sums as packed f32x2 operations, the sign
+// of q kept for an exact zero, and cvt.rn.satfinite.e4m3x2.f32 encoding the
+// pair. Scales that are zero, negative zero or non-finite, or
+// whose reciprocal is not finite, take the IEEE division per element.
+constexpr int kRowU = 2;
+
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// copysign(min(|q|, 1e4), q) with NaN kept: every quotient beyond +-464
+// saturates to the same +-448 code, and the bound keeps the exact correction
+// below finite (an infinite q would turn it into NaN).
+__device__ __forceinline__ float clamp_q(float q) {
+  float d;
+  asm("min.NaN.xorsign.abs.f32 %0, %1, 0f461C4000;" : "=f"(d) : "f"(q));
+  return d;
+}
+
+template <typename T>
+__device__ __forceinline__ void pair_to_f32(uint32_t w, float& lo, float& hi) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xFFFF0000u);
+  } else {
+    const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    lo = v.x;
+    hi = v.y;
+  }
+}
+
+struct RowScale {
+  uint64_t s2n, y2;   // (-s, -s), (y, y) with y = RN(1/s)
+  float s;
+  bool fast;          // Markstein path valid for this scale
+};
+
+template <typename T>
+__device__ __forceinline__ RowScale row_scale(float s) {
+  RowScale r;
+  const float y = __frcp_rn(s);
+  r.s = s;
+  r.fast = isfinite(s) && s != 0.f && isfinite(y) && y != 0.f;
+  r.s2n = pk2(-s, -s);
+  r.y2 = pk2(y, y);
+  return r;
+}
+
+// 8 inputs (one 16-byte vector) -> 8 E4M3 codes of RN(x / s).
+template <typename T>
+__device__ __forceinline__ uint2 e4m3x8(const uint4& raw, const RowScale& rs) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t c16[4];
+  if (rs.fast) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x0, x1, q0, q1, d0, d1;
+      pair_to_f32<T>(w[i], x0, x1);
+      const uint64_t x2 = pk2(x0, x1);
+      upk2(mul2(x2, rs.y2), q0, q1);
+      const uint64_t q2 = pk2(clamp_q(q0), clamp_q(q1));
+      const uint64_t r2 = fma2(q2, rs.s2n, x2);  // x - q s, exact
+      upk2(fma2(r2, rs.y2, q2), d0, d1);
+      upk2(q2, q0, q1);
+      c16[i] = e4m3x2_sat(copysignf(d0, q0), copysignf(d1, q1));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float x0, x1;
+      pair_to_f32<T>(w[i], x0, x1);
+      c16[i] = e4m3x2_sat(__fdiv_rn(x0, rs.s), __fdiv_rn(x1, rs.s));
+    }
+  }
+  return make_uint2(c16[0] | (c16[1] << 16), c16[2] | (c16[3] << 16));
+}
+
+template <typename T, bool FP8, int NV>
+__global__ void __launch_bounds__(256) store_row_kernel(StoreArgs a) {
+  const StoreSide& s = a.side[blockIdx.y];
+  if (s.x == nullptr) return;
+  constexpr int VEC = 8;
+  const int lane = threadIdx.x & 31;
+  const int chunks = s.D / VEC;
+  const int nvec = s.H * chunks;
+  int32_t soff[NV], doff[NV];
+  RowScale rsc[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int v = k * 32 + lane;
+    const int h = v < nvec ? v / chunks : 0;
+    const int c = v - h * chunks;
+    soff[k] = v < nvec ? (int32_t)(h * s.xs1 + c * VEC) : -1;
+    doff[k] = (int32_t)(h * s.cs2 + c * VEC);
+    if constexpr (FP8) rsc[k] = row_scale<T>(s.scale ? __ldg(s.scale + h * s.scale_stride) : 1.f);
+  }
+  const T* x = reinterpret_cast<const T*>(s.x);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < s.tokens;
+       t += warps * kRowU) {
+    int64_t slot[kRowU];
+    uint4 raw[kRowU][NV];
+#pragma unroll
+    for (int u = 0; u < kRowU; ++u) {
+      const int64_t tt = t + u * warps;
+      slot[u] = tt < s.tokens ? load_index(a.slots, a.slot_dtype, tt * a.slot_stride) : -1;
+#pragma unroll
+      for (int k = 0; k < NV; ++k)
+        if (tt < s.tokens && soff[k] >= 0)
+          raw[u][k] = __ldg(reinterpret_cast<const uint4*>(x + tt * s.xs0 + soff[k]));
+    }
+#pragma unroll
+    for (int u = 0; u < kRowU; ++u) {
+      if (slot[u] < 0 || slot[u] >= s.capacity) continue;
+      const int64_t block = page_of(slot[u], s.P, s.pshift), off = slot[u] - block * s.P;
+      const int64_t drow = block * s.cs0 + off * s.cs1;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        if (soff[k] < 0) continue;
+        if constexpr (FP8) {
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(s.cache) + drow + doff[k]) =
+              e4m3x8<T>(raw[u][k], rsc[k]);
+        } else {
+          *reinterpret_cast<uint4*>(reinterpret_cast<T*>(s.cache) + drow + doff[k]) = raw[u][k];
+        }
+      }
+    }
+  }
+}
+
 bool aligned(const void* p, int64_t bytes) { return ((uintptr_t)p % bytes) == 0; }
 
 // One side (K or V) of a store call: shape checks and vector eligibility.
@@ -233,9 +388,40 @@ int prepare_side(const fa_tensor* x, const fa_tensor* cache, const fa_tensor* sc
   return FA_OK;
 }
 
+// Vectors per lane of the row kernel for this side, or 0 when it does not apply
+// (16-bit inputs, whole 16-byte vectors, a row of at most 32 * 8 vectors,
+// offsets within a row below 2^31).
+template <typename T>
+int row_vectors(const StoreSide& s) {
+  if (sizeof(T) != 2) return 0;
+  const int64_t nvec = (int64_t)s.H * (s.D / 8);
+  if (nvec <= 0 || nvec > 32 * 8) return 0;
+  if ((int64_t)s.H * s.xs1 + s.D >= (1LL << 31) || (int64_t)s.H * s.cs2 + s.D >= (1LL << 31)) return 0;
+  const int64_t nv = (nvec + 31) / 32;
+  return nv <= 1 ? 1 : nv <= 2 ? 2 : nv <= 4 ? 4 : 8;
+}
+
 template <typename T, bool FP8>
 void launch_store(const StoreArgs& a, bool vec, int sides, cudaStream_t stream) {
   const StoreSide& s0 = a.side[0].x ? a.side[0] : a.side[1];
+  int nv = vec ? row_vectors<T>(s0) : 0;
+  if (nv && a.side[0].x && a.side[1].x && row_vectors<T>(a.side[1]) != nv) nv = 0;
+  if constexpr (sizeof(T) == 2) if (nv) {
+    // One warp per token row, kRowU rows in flight per warp.
+    int64_t blocks = (s0.tokens + 8 * kRowU - 1) / (8 * kRowU);
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    dim3 grid((unsigned)blocks, (unsigned)sides);
+    switch (nv) {
+      case 1: store_row_kernel<T, FP8, 1><<<grid, 256, 0, stream>>>(a); break;
+      case 2: store_row_kernel<T, FP8, 2><<<grid, 256, 0, stream>>>(a); break;
+      case 4: store_row_kernel<T, FP8, 4><<<grid, 256, 0, stream>>>(a); break;
+      default: store_row_kernel<T, FP8, 8><<<grid, 256, 0, stream>>>(a); break;
+    }
+    note_launch();
+    return;
+  }
   const int per_token = s0.H * (vec ? s0.D / Vec16<T>::N : s0.D);  // both sides share H, D
   int bx = (per_token + 31) / 32 * 32;
   if (bx > 256) bx = 256;

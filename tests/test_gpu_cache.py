@@ -91,6 +91,30 @@ def test_fp8_exhaustive_against_torch_cast(device, src_dtype):
     np.testing.assert_array_equal(codes, expected.view(torch.uint8).numpy())
 
 
+@pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float16])
+def test_fp8_row_path_specials_and_extreme_scales(device, src_dtype):
+    # 16-bit rows of one token per warp (the row kernel): infinities, NaNs,
+    # signed zeros, the largest finite values and subnormals under scales that
+    # make the products overflow or underflow, plus zero, negative and
+    # non-finite scales (IEEE division per element). Bit-exact with torch's
+    # cast of clamp(x / scale, -448, 448).
+    info = torch.finfo(src_dtype)
+    vals = torch.tensor([0., -0., float("inf"), -float("inf"), float("nan"), info.max, -info.max,
+                         info.tiny, -info.tiny, info.tiny / 4, 1.0, -1.0, 447.5, 464., -465., 3e-3],
+                        dtype=torch.float32).to(src_dtype)
+    scale = torch.tensor([1e-30, 1e30, 0.0, -0.5, -3.0 / 448.0, float("inf"), 2.0 ** -20, 1.0 / 448.0],
+                         dtype=torch.float32)
+    heads, dim = scale.numel(), 16
+    rows = vals.reshape(1, 1, -1).expand(3, heads, dim).contiguous()
+    cache = torch.empty((3, 1, heads, dim), dtype=torch.float8_e4m3fn, device=device)
+    store_kvcache(rows.to(device), rows.to(device), cache, cache, torch.arange(3, device=device),
+                  k_scale=scale.to(device), v_scale=scale.to(device))
+    expected = (rows.to(device).float() / scale.to(device)[None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    got, want = cache.view(torch.uint8)[:, 0], expected.view(torch.uint8)
+    bad = (got != want).nonzero().tolist()
+    assert not bad, [(scale[h].item(), vals[d].item(), int(got[t, h, d]), int(want[t, h, d])) for t, h, d in bad[:8]]
+
+
 def test_fp8_random_float32_quotients_round_exactly(device):
     # Full-mantissa float32 inputs over a wide exponent range and inexact
     # per-head scales: codes equal torch's cast of the IEEE quotient.
