@@ -767,6 +767,67 @@ def run_store(peaks, peak_kind, steps=20, warmup=3, fp8=True, tokens=524288, min
                          "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} hbm_gbs"}}
 
 
+def run_rope_append(peaks, peak_kind, steps=20, warmup=3, requests=16, tokens=1024, min_seconds=0.0):
+    """Fused RoPE + paged append (what flash_attn_with_kvcache does before
+    attention in config 5's prefill): Q [B, S, 16, 128] rotated into a new
+    tensor, K rotated and V appended at positions 0..S-1 of a page-16 bf16
+    cache through a seeded page permutation, split-half pairs, fp32 cos/sin.
+    Algorithmic bytes: Q, K, V read once, rotated Q and the K/V cache rows
+    written once, the cos/sin rows of the S positions read once. Checks a
+    sample of tokens bit for bit against torch's fp32 rotation."""
+    import torch
+    from flash_attn_b200._cache import rotary_append_kvcache
+    dev = torch.device("cuda")
+    B, S, HQ, HK, D, P = requests, tokens, 16, 8, 128, 16
+    g = torch.Generator(device=dev).manual_seed(13)
+    q = torch.randn(B, S, HQ, D, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, S, HK, D, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, S, HK, D, device=dev, generator=g).to(torch.bfloat16)
+    pages = S // P
+    gen = torch.Generator(device="cpu").manual_seed(14)
+    table = torch.randperm(B * pages, generator=gen).to(torch.int32).reshape(B, pages).to(dev)
+    kc = torch.zeros(B * pages, P, HK, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    inv = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=dev).float() / D))
+    ang = torch.arange(S, device=dev).float()[:, None] * inv[None, :]
+    cos, sin = ang.cos(), ang.sin()
+    lengths = torch.zeros(B, dtype=torch.int32, device=dev)
+    box = []
+
+    def call():
+        box[:] = [rotary_append_kvcache(q, k, v, kc, vc, cos, sin, lengths, rotary_interleaved=False,
+                                        causal=True, block_table=table)]
+
+    timed = time_loop(call, steps, warmup, min_seconds)
+    ms, steps = timed if isinstance(timed, tuple) else (timed, steps)
+    torch.cuda.synchronize()
+
+    def rope(x, pos):
+        xf = x.float()
+        h = D // 2
+        c, s_ = cos[pos][:, None, :], sin[pos][:, None, :]
+        x1, x2 = xf[..., :h], xf[..., h:]
+        return torch.cat((x1 * c - x2 * s_, x2 * c + x1 * s_), dim=-1).to(torch.bfloat16)
+
+    pos = torch.arange(0, S, 97, device=dev)
+    for b in (0, B - 1):
+        want_q = rope(q[b, pos], pos)
+        if not torch.equal(box[0][b, pos], want_q):
+            raise AssertionError("rotated q differs from torch's fp32 rotation")
+        slots = table[b, pos // P].long() * P + pos % P
+        if not torch.equal(kc.view(-1, HK, D)[slots], rope(k[b, pos], pos)):
+            raise AssertionError("appended rotated K differs from torch's fp32 rotation")
+        if not torch.equal(vc.view(-1, HK, D)[slots], v[b, pos]):
+            raise AssertionError("appended V differs")
+    nbytes = 2 * (q.numel() + k.numel() + v.numel()) * 2 + 2 * cos.numel() * 4
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"workload": f"fused RoPE + paged append, {B} x {S} new tokens, 16q/8kv heads, D=128, page 16, bf16",
+            "bytes_per_step": nbytes, "ms_per_step": ms, "steps": steps, "TB/s": gbs / 1e3,
+            "parity": {"status": "ok", "against": "torch fp32 rotation (bit-exact), sampled tokens"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": gbs / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} hbm_gbs"}}
+
+
 def run_serving(peaks, peak_kind, steps=2, warmup=3, small=False, path="fused", cpu_baseline=False):
     """Config 5: Qwen3-0.6B-shaped serving loop, attention through the library.
 
@@ -1029,7 +1090,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
-                                           "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16"],
+                                           "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16",
+                                           "rope_append"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -1071,6 +1133,10 @@ def main():
             elif args.workload == "prefill_fp8kv":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)
                 value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload == "rope_append":
+                r = run_rope_append(peaks, peak_kind, steps=args.steps, warmup=args.warmup,
+                                    requests=4 if args.small else 16)
+                value, unit = r["TB/s"], "TB/s"
             elif args.workload in ("store_fp8", "store_bf16"):
                 r = run_store(peaks, peak_kind, steps=args.steps, warmup=args.warmup,
                               fp8=args.workload == "store_fp8", tokens=65536 if args.small else 524288)
@@ -1105,7 +1171,8 @@ def main():
         if world == 1 and not args.no_secondary and not args.small:
             secondaries = [
                 ("serving_cfg5", lambda: run_serving(peaks, peak_kind)),
-                ("store_kvcache_fp8", lambda: rested(lambda: run_store(peaks, peak_kind, min_seconds=1.0), 0.5)),
+                ("store_kvcache_fp8", lambda: rested(lambda: run_store(peaks, peak_kind, min_seconds=0.3), 0.5)),
+                ("rope_append", lambda: rested(lambda: run_rope_append(peaks, peak_kind, min_seconds=0.3), 0.5)),
                 ("decode_cfg3", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=1.2))),
                 ("prefill_cfg2_fp8kv", lambda: rested(lambda: run_prefill(peaks, peak_kind, fp8_kv=True,
                                                                           min_seconds=0.15))),

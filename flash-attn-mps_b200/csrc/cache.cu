@@ -15,6 +15,7 @@
 // quotients take the IEEE division. Pairs are encoded with the packed
 // cvt.rn.satfinite.e4m3x2.f32. append / rotary: one element or 16-byte vector
 // per thread with a grid-stride loop.
+#include <algorithm>
 #include <type_traits>
 
 #include "common.cuh"
@@ -796,6 +797,161 @@ __global__ void __launch_bounds__(128) rope_append_vec_kernel(VecArgs a) {
   }
 }
 
+// Warp-per-token-row variant of rope_append_vec_kernel (same arithmetic, same
+// results bit for bit). A warp owns one (token, head group) of one side at a
+// time; lane L takes one column group c = L % U of a head (U = column groups
+// per head: a rotated split-half pair (c, c + half), or one 16-byte vector) for
+// MAXU heads of the group, 32 / U apart, so its cos/sin columns are loaded
+// once per item. The input vectors do not depend on the request's length or
+// page table and are loaded first; the length of the warp's next item is
+// prefetched while the current one is written. Rows wider than 32 * MAXU
+// column groups (16 query heads of 128 dims) take several warps, which keeps
+// the kernel at 80 registers (3 CTAs per SM).
+template <typename T, int MAXU, bool FP8>
+__global__ void __launch_bounds__(256) rope_append_warp_kernel(VecArgs a) {
+  const int which = blockIdx.y;
+  const VecSide& s = a.side[which];
+  if (s.x == nullptr) return;
+  const int lane = threadIdx.x & 31;
+  const bool split = s.rotate && !a.interleaved;
+  const int r2 = split ? a.half / 8 : 0;  // rotated pairs per head
+  const int uph = s.V - r2;               // column groups per head (divides 32)
+  const int c = lane % uph, hstep = 32 / uph;
+  // A token row is split into head groups of 32 * MAXU / uph heads; a warp
+  // work item is one (token, head group).
+  const int group_heads = hstep * MAXU;
+  const int groups = (s.H + group_heads - 1) / group_heads;
+  const int64_t items = a.tokens * groups;
+  const bool pair = split && c < r2;
+  const int c0 = split && !pair ? (r2 + c) * 8 : c * 8;
+  const bool rot = s.rotate && (split ? pair : c0 < 2 * a.half);
+  const bool fp8 = FP8 && s.fp8;  // FP8 = some side writes an FP8 cache
+  const int64_t dst_elt = which != 2 && fp8 ? 1 : (int64_t)sizeof(T);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  auto split_tok = [&](int64_t t, int64_t& b, int& j) {
+    b = t <= 0x7fffffff ? (int64_t)((uint32_t)t / (uint32_t)a.S) : t / a.S;
+    j = (int)(t - b * a.S);
+  };
+  int64_t item = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int64_t b = 0;
+  int j = 0, hbase = 0;
+  int64_t len = 0;
+  auto split_item = [&](int64_t w, int64_t& bb, int& jj, int& hb) {
+    const int64_t t = groups == 1 ? w : w / groups;
+    hb = (int)(w - t * groups) * group_heads + lane / uph;
+    split_tok(t, bb, jj);
+  };
+  if (item < items) {
+    split_item(item, b, j, hbase);
+    len = a.lengths[b * a.len_stride];
+  }
+  for (; item < items; item += warps) {
+    const uint8_t* in_tok = s.x + (b * s.xs0 + j * s.xs1) * (int64_t)sizeof(T);
+    uint4 xa[MAXU], xb[MAXU];
+#pragma unroll
+    for (int k = 0; k < MAXU; ++k) {
+      const int h = hbase + k * hstep;
+      if (h < s.H) {
+        const uint8_t* in = in_tok + h * s.xs2 * (int64_t)sizeof(T);
+        xa[k] = __ldg(reinterpret_cast<const uint4*>(in + (int64_t)c0 * sizeof(T)));
+        if (pair) xb[k] = __ldg(reinterpret_cast<const uint4*>(in + (int64_t)(c0 + a.half) * sizeof(T)));
+      }
+    }
+    // Row geometry of this token; the next item's length is loaded meanwhile.
+    int64_t nb = 0, nlen = 0;
+    int nj = 0, nhbase = 0;
+    if (item + warps < items) {
+      split_item(item + warps, nb, nj, nhbase);
+      nlen = a.lengths[nb * a.len_stride];
+    }
+    int64_t pos;
+    uint8_t* out_tok = nullptr;
+    if (which == 2) {
+      pos = len + (a.advance_q ? j : 0);
+      out_tok = s.dst + (b * s.ds0 + j * s.ds1) * dst_elt;
+    } else {
+      pos = len + j;
+      const int64_t row = a.remap ? (int64_t)a.batch_idx[b * a.bi_stride] : b;
+      const int64_t capacity = a.paged ? (int64_t)a.pages_per_seq * a.P : a.P;
+      if (row >= 0 && row < a.rows && pos >= 0 && pos < capacity) {
+        int64_t block = row, offset = pos;
+        if (a.paged) {
+          const int64_t pg = a.pshift >= 0 ? (pos >> a.pshift) : pos / a.P;
+          block = a.table[row * a.bt0 + pg * a.bt1];
+          offset = pos - pg * a.P;
+        }
+        if (block >= 0 && block < a.blocks) out_tok = s.dst + (block * s.ds0 + offset * s.ds1) * dst_elt;
+      }
+    }
+    if (out_tok != nullptr) {
+      float cc[8], ss[8];
+      if (rot) {
+        if (split) {
+          const float4* cp = reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0);
+          const float4* sp = reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0);
+          const float4 ca = __ldg(cp), cb = __ldg(cp + 1), sa = __ldg(sp), sb = __ldg(sp + 1);
+          cc[0] = ca.x; cc[1] = ca.y; cc[2] = ca.z; cc[3] = ca.w; cc[4] = cb.x; cc[5] = cb.y; cc[6] = cb.z; cc[7] = cb.w;
+          ss[0] = sa.x; ss[1] = sa.y; ss[2] = sa.z; ss[3] = sa.w; ss[4] = sb.x; ss[5] = sb.y; ss[6] = sb.z; ss[7] = sb.w;
+        } else {
+          const float4 cv = __ldg(reinterpret_cast<const float4*>(a.cos + pos * a.cs0 + c0 / 2));
+          const float4 sv = __ldg(reinterpret_cast<const float4*>(a.sin + pos * a.ss0 + c0 / 2));
+          cc[0] = cv.x; cc[1] = cv.y; cc[2] = cv.z; cc[3] = cv.w;
+          ss[0] = sv.x; ss[1] = sv.y; ss[2] = sv.z; ss[3] = sv.w;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < MAXU; ++k) {
+        const int h = hbase + k * hstep;
+        if (h >= s.H) continue;
+        uint8_t* out = out_tok + h * s.ds2 * dst_elt;
+        const float scale = fp8 && s.scale ? s.scale[h * s.scale_stride] : 1.0f;
+        if (!rot) {
+          if (!fp8) {
+            *reinterpret_cast<uint4*>(out + (int64_t)c0 * sizeof(T)) = xa[k];
+          } else {
+            float f[8];
+            unpack8<T>(xa[k], f);
+            put8<T>(s, out, c0, f, scale);
+          }
+        } else if (split) {
+          float x1[8], x2[8], o1[8], o2[8];
+          unpack8<T>(xa[k], x1);
+          unpack8<T>(xb[k], x2);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            o1[i] = __fadd_rn(__fmul_rn(x1[i], cc[i]), -__fmul_rn(x2[i], ss[i]));
+            o2[i] = __fadd_rn(__fmul_rn(x2[i], cc[i]), __fmul_rn(x1[i], ss[i]));
+          }
+          put8<T>(s, out, c0, o1, scale);
+          put8<T>(s, out, c0 + a.half, o2, scale);
+        } else {
+          float x[8], o[8];
+          unpack8<T>(xa[k], x);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            o[2 * i] = __fadd_rn(__fmul_rn(x[2 * i], cc[i]), -__fmul_rn(x[2 * i + 1], ss[i]));
+            o[2 * i + 1] = __fadd_rn(__fmul_rn(x[2 * i + 1], cc[i]), __fmul_rn(x[2 * i], ss[i]));
+          }
+          put8<T>(s, out, c0, o, scale);
+        }
+      }
+    }
+    b = nb;
+    j = nj;
+    hbase = nhbase;
+    len = nlen;
+  }
+}
+
+// Whether the warp kernel applies to this side: its column groups per head
+// must divide 32 (rows wider than 64 column groups are split over warps).
+bool warp_fits(const VecSide& s, const VecArgs& a) {
+  if (!s.x) return true;
+  const int r2 = s.rotate && !a.interleaved ? a.half / 8 : 0;
+  const int uph = s.V - r2;
+  return uph > 0 && 32 % uph == 0;
+}
+
 inline bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
 inline int log2_exact(int64_t v) {
@@ -865,6 +1021,28 @@ int launch_rope_append_vec(const AppendArgs& a, const RopeArgs* r, int64_t batch
       work = work || (int64_t)v.side[i].H * v.side[i].V > 0;
     }
   if (v.tokens == 0 || !work) return FA_OK;
+  bool fits = true;
+  for (int i = 0; i < 3; ++i) fits = fits && warp_fits(v.side[i], v);
+  if (fits) {
+    const bool fp8 = (v.side[0].x && v.side[0].fp8) || (v.side[1].x && v.side[1].fp8);
+    const bool bf = dtype == FA_BF16;
+    // Two heads per lane at most: wider rows take several warps per token.
+    auto kernel = bf ? (fp8 ? rope_append_warp_kernel<__nv_bfloat16, 2, true> : rope_append_warp_kernel<__nv_bfloat16, 2, false>)
+                     : (fp8 ? rope_append_warp_kernel<__half, 2, true> : rope_append_warp_kernel<__half, 2, false>);
+    // One warp per token row (8 per CTA); the grid holds exactly the CTAs that
+    // are resident at once (all sides together), each looping over tokens.
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    int64_t cap = (int64_t)sm_count() * per_sm / sides;
+    if (cap < 1) cap = 1;
+    const int64_t want = (v.tokens * 2 + 7) / 8;
+    const dim3 grid((unsigned)(want < cap ? want : cap), sides);
+    kernel<<<grid, 256, 0, stream>>>(v);
+    note_launch();
+    FAB_LAUNCH_CHECK("vectorized append launch");
+    return FA_OK;
+  }
   const int64_t cap = (int64_t)sm_count() * 16;
   const dim3 grid((unsigned)(v.tokens < cap ? v.tokens : cap), sides);
   if (dtype == FA_BF16) rope_append_vec_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(v);
