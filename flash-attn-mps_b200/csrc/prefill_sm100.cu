@@ -130,6 +130,7 @@ struct PrefillParams {
   int32_t bt_cols, page_shift, box_rows;   // page = 1 << page_shift tokens, box_rows = min(page, 128)
   const float* alibi; int64_t al0, al1;    // ALiBi slopes [B,H] or [H] (ALIBI instantiation only)
   int32_t dim;                             // true head dim (<= HDIM; columns past it are TMA zero fill)
+  int32_t head_pairs;                      // 1: tiles A/B = query heads h, h+1 of one row block; 0: row blocks r, r+1
   int32_t B, HQ, HK, n_pairs, causal, win_l, win_r;
   float scale, softcap;
 };
@@ -284,9 +285,13 @@ __device__ __forceinline__ void tile_range(int row0, int q_len, int k_len, bool 
   *last = z.hi / BN + 1;
 }
 
-// One work item: a pair of 128-row query tiles of one (request, query head).
-// Items are ordered by pair index descending (the costliest causal tiles
-// first), then head, then request.
+// One work item: two 128-row query tiles (A, B) of one request. When the
+// query heads per KV head are even, A and B are the same row block of query
+// heads h and h+1, which share their KV head: both see exactly the same key
+// tiles (the same K/V loads, the same causal extent), so neither tile idles
+// while the other finishes a diagonal or a short sequence. Otherwise A and B
+// are row blocks r and r+1 of one head. Items are ordered by row-block index
+// descending (the costliest causal tiles first), then head, then request.
 // The TMA warp decodes each claimed item once (including its global reads:
 // sequence offsets, lengths, causal flag, descales, sink) and publishes it in
 // shared memory, so the MMA and softmax warps start an item without any
@@ -294,7 +299,8 @@ __device__ __forceinline__ void tile_range(int row0, int q_len, int k_len, bool 
 struct Item {
   int valid, b, h, kh, q_begin, q_len, k_begin, k_len, row_a, row_b, causal;
   int a0, a1, b0, b1, j_first, n_all;
-  float qk_scale, vscale, sink_l2;  // sink_l2: sink logit in log2 units, -inf without one
+  float qk_scale, vscale;
+  int h_b;  // query head of tile B
 };
 constexpr int kItemWords = sizeof(Item) / 4;
 static_assert(sizeof(Item) == 20 * 4, "Item is 20 words");
@@ -305,7 +311,7 @@ __device__ __forceinline__ void item_store(volatile int* d, const Item& it) {
   d[0] = it.valid; d[1] = it.b; d[2] = it.h; d[3] = it.kh; d[4] = it.q_begin; d[5] = it.q_len;
   d[6] = it.k_begin; d[7] = it.k_len; d[8] = it.row_a; d[9] = it.row_b; d[10] = it.causal;
   d[11] = it.a0; d[12] = it.a1; d[13] = it.b0; d[14] = it.b1; d[15] = it.j_first; d[16] = it.n_all;
-  d[17] = __float_as_int(it.qk_scale); d[18] = __float_as_int(it.vscale); d[19] = __float_as_int(it.sink_l2);
+  d[17] = __float_as_int(it.qk_scale); d[18] = __float_as_int(it.vscale); d[19] = it.h_b;
 }
 // Five 16-byte shared loads (issued together) after the slot's full barrier.
 __device__ __forceinline__ void item_load(const volatile int* d, Item& it) {
@@ -322,26 +328,27 @@ __device__ __forceinline__ void item_load(const volatile int* d, Item& it) {
   it.row_a = w[2].x; it.row_b = w[2].y; it.causal = w[2].z; it.a0 = w[2].w;
   it.a1 = w[3].x; it.b0 = w[3].y; it.b1 = w[3].z; it.j_first = w[3].w;
   it.n_all = w[4].x; it.qk_scale = __int_as_float(w[4].y); it.vscale = __int_as_float(w[4].z);
-  it.sink_l2 = __int_as_float(w[4].w);
+  it.h_b = w[4].w;
 }
 
 __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   Item it;
-  const int per = p.HQ * p.B;
+  const int hsteps = p.HQ >> p.head_pairs;  // query heads, or head pairs
+  const int per = hsteps * p.B;
   const int pair = p.n_pairs - 1 - w / per;
   const int rem = w - (w / per) * per;
-  it.h = rem % p.HQ;
-  it.b = rem / p.HQ;
+  it.h = (rem % hsteps) << p.head_pairs;
+  it.h_b = it.h + p.head_pairs;
+  it.b = rem / hsteps;
   it.q_begin = p.cu_q[it.b * p.cq0];
   it.q_len = p.cu_q[(it.b + 1) * p.cq0] - it.q_begin;
-  it.row_a = pair * 2 * BM;
-  it.row_b = it.row_a + BM;
+  it.row_a = pair * (p.head_pairs ? BM : 2 * BM);
+  it.row_b = it.row_a + (p.head_pairs ? 0 : BM);
   it.valid = it.row_a < it.q_len;
   it.n_all = 0;
   it.a0 = it.a1 = it.b0 = it.b1 = it.j_first = 0;
   it.k_begin = it.k_len = it.kh = it.causal = 0;
   it.qk_scale = it.vscale = 1.f;
-  it.sink_l2 = -INFINITY;
   if (!it.valid) return it;
   it.k_begin = p.cu_k ? p.cu_k[it.b * p.ck0] : 0;
   it.k_len = p.used ? p.used[it.b * p.u0] : p.cu_k[(it.b + 1) * p.ck0] - it.k_begin;
@@ -350,7 +357,6 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   it.qk_scale = p.scale * (p.qd ? p.qd[it.b * p.qd0 + it.kh * p.qd1] : 1.f) *
                 (p.kd ? p.kd[it.b * p.kd0 + it.kh * p.kd1] : 1.f);
   it.vscale = p.vd ? p.vd[it.b * p.vd0 + it.kh * p.vd1] : 1.f;
-  if (p.sinks) it.sink_l2 = load_float(p.sinks, p.sink_t, it.h * p.si0) * 1.4426950408889634f;
   tile_range(it.row_a, it.q_len, it.k_len, it.causal, p.win_l, p.win_r, &it.a0, &it.a1);
   tile_range(it.row_b, it.q_len, it.k_len, it.causal, p.win_l, p.win_r, &it.b0, &it.b1);
   const bool ha = it.a1 > it.a0, hb = it.b1 > it.b0;
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_work = p.n_pairs * p.HQ * p.B;
+  const int n_work = p.n_pairs * (p.HQ >> p.head_pairs) * p.B;
   auto bar = [&](int i) { return base + OFF_BAR + 8u * (uint32_t)i; };
   const uint32_t holder = base + OFF_BAR + 8u * B_COUNT;
   volatile uint32_t* holder_ptr = reinterpret_cast<volatile uint32_t*>(gbase + OFF_BAR + 8 * B_COUNT);
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int hf = 0; hf < kHalves; ++hf) {
           tma_load_3d(base + OFF_QA + hf * kRegion, &tq, bar(B_Q), hf * 64, it.h, it.q_begin + it.row_a);
-          tma_load_3d(base + OFF_QB + hf * kRegion, &tq, bar(B_Q), hf * 64, it.h, it.q_begin + it.row_b);
+          tma_load_3d(base + OFF_QB + hf * kRegion, &tq, bar(B_Q), hf * 64, it.h_b, it.q_begin + it.row_b);
         }
       }
       ++qloads;
@@ -640,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q_row = (is_b ? it.row_b : it.row_a) + row;
       const int q_abs = q_row + it.k_len - it.q_len;
       const KeyRange vis = key_range(q_abs, it.k_len, it.causal, p.win_l, p.win_r);
-      const int h = it.h;
+      const int h = is_b ? it.h_b : it.h;
       const float qk_scale = it.qk_scale, vscale = it.vscale;
       const float sl2 = qk_scale * 1.4426950408889634f;     // raw score -> log2 units
       // ALiBi slope in log2 units; with ALiBi the scores are biased (and thus
@@ -650,7 +656,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float cap_l2 = p.softcap * 1.4426950408889634f;  // softcap: cap*log2e*tanh(s*scale/cap)
       const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
       // Running max in log2 units; a sink acts as one extra logit with zero value.
-      float m_run = it.sink_l2, l_run = p.sinks ? 1.f : 0.f;
+      float m_run = p.sinks ? load_float(p.sinks, p.sink_t, h * p.si0) * 1.4426950408889634f : -INFINITY;
+      float l_run = p.sinks ? 1.f : 0.f;
       for (int jj = 0; jj < n_x; ++jj) {
         const int j = x0 + jj;
         const int sbuf = (int)(s_cnt % SBUF);
@@ -931,7 +938,7 @@ int prefill_sm100_supported(const AttnParams& p) {
     if (v <= 0 || (v * 2) % 16 != 0) return 0;
   if (p.T >= (1 << 30)) return 0;
   if (!p.paged && (p.k_rows <= 0 || p.k_rows >= (1 << 30))) return 0;
-  if ((int64_t)((p.max_q + 2 * BM - 1) / (2 * BM)) * p.HQ * p.B >= (1LL << 31)) return 0;
+  if ((int64_t)((p.max_q + BM - 1) / BM) * p.HQ * p.B >= (1LL << 31)) return 0;
   if (!tensor_map_available()) return 0;
   return 1;
 }
@@ -981,7 +988,9 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
     pp.table = p.table; pp.bt0 = p.bt0; pp.bt1 = p.bt1;
     pp.bt_cols = (int32_t)p.bt_cols; pp.page_shift = page_shift; pp.box_rows = box_rows;
   }
-  pp.n_pairs = (p.max_q + 2 * BM - 1) / (2 * BM);
+  // Pair query heads h, h+1 (same KV head) when the heads per KV head are even.
+  pp.head_pairs = (p.HQ / p.HK) % 2 == 0 ? 1 : 0;
+  pp.n_pairs = pp.head_pairs ? (p.max_q + BM - 1) / BM : (p.max_q + 2 * BM - 1) / (2 * BM);
   pp.causal = p.causal;
   pp.causal_b = p.dynamic ? p.causal_b : nullptr; pp.ca0 = p.ca0;
   pp.sinks = p.sinks; pp.sink_t = p.sink_t; pp.si0 = p.si0;
@@ -1013,7 +1022,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   if (fa.numRegs != kLaunchRegs)
     return fail(FA_ERR_CUDA, "prefill kernel built with %d registers per thread, expected %d", fa.numRegs,
                 kLaunchRegs);
-  const int64_t n_work = (int64_t)pp.n_pairs * p.HQ * p.B;
+  const int64_t n_work = (int64_t)pp.n_pairs * (p.HQ >> pp.head_pairs) * p.B;
   const int grid = (int)std::min<int64_t>(n_work, (int64_t)sm_count());
   if (pp.counter == nullptr) return fail(FA_ERR_INVALID, "prefill needs its workspace counter");
   e = cudaMemsetAsync(pp.counter, 0, sizeof(int), stream);
