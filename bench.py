@@ -520,7 +520,7 @@ def cfg2_lengths(cfg):
     return rng.integers(cfg["lmin"], cfg["lmax"] + 1, size=cfg["seqs"]).tolist()
 
 
-def cfg2_flops(lengths, cfg, window=-1):
+def cfg2_flops(lengths, cfg, window=-1, dims=None):
     pairs = 0
     for L in lengths:
         if window < 0:
@@ -528,7 +528,8 @@ def cfg2_flops(lengths, cfg, window=-1):
         else:
             w = window + 1
             pairs += sum(min(i + 1, w) for i in range(L))
-    return cfg["hq"] * (2 * cfg["d"] + 2 * cfg["d"]) * pairs
+    dq, dv = dims if dims else (cfg["d"], cfg["d"])
+    return cfg["hq"] * (2 * dq + 2 * dv) * pairs
 
 
 def rested(measure, pause=2.0):
@@ -574,7 +575,7 @@ def time_loop(fn, steps, warmup, min_seconds=0.0):
 
 
 def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -1), small=False, fp8_kv=False,
-                kv_slice=None, alibi=False, min_seconds=0.0, sustained=False):
+                kv_slice=None, alibi=False, min_seconds=0.0, sustained=False, dims=None):
     """Config 2: varlen causal prefill bf16 through flash_attn_varlen_func.
 
     ``fp8_kv``: the same lengths over FP8 E4M3 K/V with per-(request, KV head)
@@ -583,6 +584,7 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     ``kv_slice=(h0, h1)``: only KV heads [h0, h1) and their query heads (one
     GPU's share when the prefill is sharded by head groups).
     ``alibi``: the standard geometric ALiBi slopes 2^(-8(h+1)/H) per query head.
+    ``dims=(dq, dv)``: other QK / V head dims (256/256, DiffKV 192/128).
     """
     import torch
     from flash_attn_b200 import flash_attn_varlen_func
@@ -594,9 +596,10 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
     total = sum(lens)
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(cfg["seed"])
-    q = torch.randn(total, cfg["hq"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
-    k = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
-    v = torch.randn(total, cfg["hkv"], cfg["d"], device=dev, generator=g).to(torch.bfloat16)
+    dq, dv = dims if dims else (cfg["d"], cfg["d"])
+    q = torch.randn(total, cfg["hq"], dq, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(total, cfg["hkv"], dq, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(total, cfg["hkv"], dv, device=dev, generator=g).to(torch.bfloat16)
     if kv_slice is not None:
         group = cfg["hq"] // cfg["hkv"]
         h0, h1 = kv_slice
@@ -604,7 +607,7 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
         k, v = k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous()
         cfg["hq"], cfg["hkv"] = (h1 - h0) * group, h1 - h0
     cu = torch.tensor([0] + list(__import__("itertools").accumulate(lens)), dtype=torch.int32, device=dev)
-    out = torch.empty_like(q)
+    out = torch.empty(total, cfg["hq"], dv, dtype=q.dtype, device=dev)
     if fp8_kv:
         k, v = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
         kd = torch.full((len(lens), cfg["hkv"]), 0.5, device=dev)
@@ -619,13 +622,14 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
                                                          out=out),
                           steps, warmup, min_seconds)
     ms, steps = timed if isinstance(timed, tuple) else (timed, steps)
-    flops = cfg2_flops(lens, cfg, window[0])
+    flops = cfg2_flops(lens, cfg, window[0], dims)
     tflops = flops / (ms * 1e-3) / 1e12
     return {"workload": "cfg2 varlen causal prefill bf16, 32 seqs L~U[64,4096], 32q/8kv, D=128"
                         + (f", softcap={softcap}, window={tuple(window)}" if softcap or window[0] >= 0 else "")
                         + (", FP8 E4M3 K/V + descales" if fp8_kv else "")
                         + (f", KV heads {kv_slice[0]}..{kv_slice[1] - 1} only" if kv_slice else "")
                         + (", ALiBi slopes" if alibi else "")
+                        + (f", head dims {dq}/{dv}" if dims else "")
                         + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "steps": steps,
             "TFLOP/s": tflops,
@@ -1091,7 +1095,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
                                            "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16",
-                                           "rope_append"],
+                                           "rope_append", "prefill_d256", "prefill_diffkv"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -1132,6 +1136,10 @@ def main():
                 value, unit = r["TFLOP/s"], "TFLOP/s"
             elif args.workload == "prefill_fp8kv":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload in ("prefill_d256", "prefill_diffkv"):
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small,
+                                dims=(256, 256) if args.workload == "prefill_d256" else (192, 128))
                 value, unit = r["TFLOP/s"], "TFLOP/s"
             elif args.workload == "rope_append":
                 r = run_rope_append(peaks, peak_kind, steps=args.steps, warmup=args.warmup,
@@ -1176,6 +1184,10 @@ def main():
                 ("decode_cfg3", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=1.2))),
                 ("prefill_cfg2_fp8kv", lambda: rested(lambda: run_prefill(peaks, peak_kind, fp8_kv=True,
                                                                           min_seconds=0.15))),
+                ("prefill_cfg2_d256", lambda: rested(lambda: run_prefill(peaks, peak_kind, dims=(256, 256),
+                                                                         min_seconds=0.15))),
+                ("prefill_cfg2_diffkv", lambda: rested(lambda: run_prefill(peaks, peak_kind, dims=(192, 128),
+                                                                           min_seconds=0.15))),
                 ("prefill_cfg2_softcap_window", lambda: rested(lambda: run_prefill(
                     peaks, peak_kind, softcap=50.0, window=(1024, 0), min_seconds=0.15))),
                 # Over a window of seconds the GPU reaches its power cap and
