@@ -648,12 +648,15 @@ def roofline_tensor(tflops, peaks, peak_kind, sustained=False):
             "frac_of_burst": tflops / burst, "frac_of_sustained": tflops / sus}
 
 
-def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False, min_seconds=0.0):
+def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False, min_seconds=0.0, d=128):
     """Config 3: paged bf16 decode, B=256, ctx ~U[512, 32768], page 16, plus a
-    sampled check of the timed output against a torch fp32 reference."""
+    sampled check of the timed output against a torch fp32 reference. With
+    d=256: the same layout at head dim 256 over 64 requests (8.8 GB of cache)."""
     import torch
     from flash_attn_b200._attention import attention
-    cfg = dict(CFG3)
+    cfg = dict(CFG3, d=d)
+    if d != 128:
+        cfg["batch"] = 64
     if small:
         cfg["batch"] = 16  # profiling case
     w = build_cfg3(cfg)
@@ -676,7 +679,7 @@ def run_bf16_decode(peaks, peak_kind, steps=50, warmup=5, small=False, min_secon
     nbytes = int(ctx.sum()) * cfg["hkv"] * 2 * cfg["d"] * 2 + int(pages_per.sum()) * 4 + 2 * w["q"].numel() * 2
     gbs = nbytes / (ms * 1e-3) / 1e9
     del w
-    return {"workload": "cfg3 paged bf16 decode, B=256, ctx~U[512,32768], page 16, 32q/8kv, D=128",
+    return {"workload": f"cfg3 paged bf16 decode, B={cfg['batch']}, ctx~U[512,32768], page 16, 32q/8kv, D={d}",
             "bytes_per_step": nbytes, "ms_per_step": ms, "steps": steps, "TB/s": gbs / 1e3,
             "parity": {"status": "ok", "requests": len(picks), "max_abs": worst},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -1095,7 +1098,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
                                            "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16",
-                                           "rope_append", "prefill_d256", "prefill_diffkv"],
+                                           "rope_append", "prefill_d256", "prefill_diffkv", "decode_d256"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
                     help="serving workload: fused RoPE+append with_kvcache calls, or store_kvcache + varlen")
@@ -1141,6 +1144,9 @@ def main():
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small,
                                 dims=(256, 256) if args.workload == "prefill_d256" else (192, 128))
                 value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload == "decode_d256":
+                r = run_bf16_decode(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, d=256)
+                value, unit = r["TB/s"], "TB/s"
             elif args.workload == "rope_append":
                 r = run_rope_append(peaks, peak_kind, steps=args.steps, warmup=args.warmup,
                                     requests=4 if args.small else 16)
@@ -1182,6 +1188,7 @@ def main():
                 ("store_kvcache_fp8", lambda: rested(lambda: run_store(peaks, peak_kind, min_seconds=0.3), 0.5)),
                 ("rope_append", lambda: rested(lambda: run_rope_append(peaks, peak_kind, min_seconds=0.3), 0.5)),
                 ("decode_cfg3", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=1.2))),
+                ("decode_d256", lambda: rested(lambda: run_bf16_decode(peaks, peak_kind, min_seconds=0.3, d=256))),
                 ("prefill_cfg2_fp8kv", lambda: rested(lambda: run_prefill(peaks, peak_kind, fp8_kv=True,
                                                                           min_seconds=0.15))),
                 ("prefill_cfg2_d256", lambda: rested(lambda: run_prefill(peaks, peak_kind, dims=(256, 256),
