@@ -460,7 +460,8 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
                                + (" (small profiling case)" if args.small else ""),
                    "batch": B, "context": C, "block_size": cfg["page"], "q_heads": HQ, "kv_heads": HK,
                    "head_dim": D, "l2": "17.2 GB cache > L2, no flush",
-                   "parallelism": f"kv-seq sharded x{world}, NCCL all-gather + merge"},
+                   "parallelism": (f"kv-seq sharded x{world}, {decoder.exchange} exchange + merge" if decoder
+                                   else "single GPU")},
         "gpu_launches": launches,
         "clocks": clocks,
         "parity": parity,

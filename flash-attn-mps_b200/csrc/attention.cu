@@ -346,8 +346,9 @@ extern "C" uint64_t fa_kernel_launches(void) { return fab::g_kernel_launches.loa
 extern "C" int fa_pipeline_timeouts(int clear) {
   const int a = fab::prefill_timeout_flag(clear != 0);
   const int b = fab::decode_timeout_flag(clear != 0);
-  if (a < 0 || b < 0) return -1;
-  return (a ? 1 : 0) | (b ? 2 : 0);
+  const int c = fab::exchange_timeout_flag(clear != 0);
+  if (a < 0 || b < 0 || c < 0) return -1;
+  return (a ? 1 : 0) | (b ? 2 : 0) | (c ? 4 : 0);
 }
 
 namespace fab {

@@ -91,5 +91,6 @@ int attention_fwd_capped(const fa_attention_args* a, void* stream, size_t part_c
 // current device (1 = some wait gave up, 0 = none, -1 = CUDA error).
 int prefill_timeout_flag(bool clear);
 int decode_timeout_flag(bool clear);
+int exchange_timeout_flag(bool clear);
 
 }  // namespace fab

@@ -80,6 +80,18 @@ SIGNATURES = {
     "fa_merge_partials": [_P(Tensor)] * 4 + [ctypes.c_void_p],
 }
 
+FA_MAX_PEERS = 8
+
+
+class PeerBuffers(ctypes.Structure):
+    _fields_ = [("slots", ctypes.c_void_p * FA_MAX_PEERS), ("flags", ctypes.c_void_p * FA_MAX_PEERS)]
+
+
+SIGNATURES.update({
+    "fa_shard_push": [_P(Tensor), _P(PeerBuffers), ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p],
+    "fa_shard_wait": [_P(PeerBuffers), ctypes.c_int32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p],
+})
+
 _lock = threading.Lock()
 _lib = None
 

@@ -5,12 +5,16 @@ paged cache (``kv_shard``). A decode step is:
 
 1. local split-KV decode over the rank's slice into an fp32 partial
    ``(out [B,Hq,Dv], lse [Hq,B])`` -- the tensor-core decode kernel plus its
-   split merge;
-2. one NCCL all-gather over NVLink / NVSwitch: each rank's out and lse sit in
-   one flat fp32 buffer (out first, then lse), so a step issues a single
-   collective and the N-way merge reads the gathered rows through strides;
+   split merge -- written as one flat fp32 row (out first, then lse);
+2. the exchange of the rows: by default one NCCL all-gather of the rows over
+   NVLink / NVSwitch; or (``exchange="p2p"``) over peer memory: the row is
+   decoded straight into this rank's slot of a gather buffer in symmetric
+   memory, the push kernel copies it into the same slot of every peer's buffer
+   and raises a per-rank flag there, and a one-warp kernel waits (bounded)
+   for every peer's flag (``fa_shard_push`` / ``fa_shard_wait``);
 3. the N-way LSE merge kernel (the same one that combines split-KV partials)
-   writes the final output in the caller's dtype on every rank.
+   reads the gathered rows through strides and writes the final output in the
+   caller's dtype on every rank.
 
 Sinks are seeded on rank 0 only, so they are counted once (the reference's
 "sink counted once" contract, tests/test_vllm.py:130-149). The reference has
@@ -18,8 +22,13 @@ no distributed code (flash_attn_mps/vllm.py:5); this composes its split-KV
 merge semantics (kernels/merge.metal:30-58) across ranks.
 """
 
+import ctypes
+import os
+
 import torch
 import torch.distributed as dist
+
+from . import _capi
 
 
 def kv_shard(length, rank, world):
@@ -53,31 +62,95 @@ def gather_partials(partial_out, partial_lse, group=None):
 class ShardedDecoder:
     """Reusable buffers for KV-sharded decode steps of a fixed batch shape.
 
-    ``packed`` holds this rank's partial state as one fp32 row
-    ``[B*Hq*Dv | Hq*B]``; ``gathered`` is ``[N, row]`` after the all-gather and
-    the merge reads its out/lse parts as strided views.
+    ``exchange="nccl"`` (the default; ``FAB_SHARD_EXCHANGE`` overrides it): the
+    row is all-gathered with NCCL into ``[N, row]``.
+    ``exchange="p2p"`` (CUDA devices, ``world > 1``): a gather buffer in
+    symmetric memory -- two parities x N slots of the packed row
+    ``[B*Hq*Dv | Hq*B]`` plus a flag array -- mapped into every rank; step e
+    decodes into this rank's slot of parity e & 1, pushes it to every peer over
+    NVLink and waits for the peers' flags before the merge.
+    The merge reads the gathered out/lse parts as strided views either way.
     """
 
-    def __init__(self, batch, q_heads, head_dim, out_dtype, device, group=None):
+    def __init__(self, batch, q_heads, head_dim, out_dtype, device, group=None, exchange=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        row = batch * q_heads * head_dim + q_heads * batch
-        self.packed = torch.empty(row, dtype=torch.float32, device=device)
-        self.partial, self.partial_lse = packed_views(self.packed, batch, q_heads, head_dim)
-        self.gathered_flat = torch.empty(self.world, row, dtype=torch.float32, device=device)
-        self.gathered, self.gathered_lse = packed_views(self.gathered_flat, batch, q_heads, head_dim)
+        self.shape = (batch, q_heads, head_dim)
+        self.row = batch * q_heads * head_dim + q_heads * batch
         self.out = torch.empty(batch, q_heads, head_dim, dtype=out_dtype, device=device)
         self.out_lse = torch.empty(q_heads, batch, dtype=torch.float32, device=device)
+        if exchange is None:
+            exchange = os.environ.get("FAB_SHARD_EXCHANGE", "nccl")
+        if self.world < 2 or torch.device(device).type != "cuda":
+            exchange = "nccl"
+        self.exchange = exchange
+        if exchange == "p2p":
+            self._init_p2p(device)
+        else:
+            self.packed = torch.empty(self.row, dtype=torch.float32, device=device)
+            self.partial, self.partial_lse = packed_views(self.packed, batch, q_heads, head_dim)
+            self.gathered_flat = torch.empty(self.world, self.row, dtype=torch.float32, device=device)
+            self.gathered, self.gathered_lse = packed_views(self.gathered_flat, batch, q_heads, head_dim)
+
+    def _init_p2p(self, device):
+        # Plain peer loads and stores only: the buffer needs no NVLink
+        # multicast object.
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        import torch.distributed._symmetric_memory as symm_mem
+        n, row = self.world, self.row
+        if n > _capi.FA_MAX_PEERS:
+            raise ValueError(f"the peer-memory exchange supports at most {_capi.FA_MAX_PEERS} ranks")
+        row_padded = (row + 63) // 64 * 64          # 256-byte aligned slots
+        data = 2 * n * row_padded
+        # The flag array (2 * FA_MAX_PEERS uint32: per-rank flags, then the push
+        # kernel's CTA counter) follows the slots in 256 spare bytes.
+        self.symm = symm_mem.empty(data + 64, dtype=torch.float32, device=device)
+        self.symm.zero_()
+        handle = symm_mem.rendezvous(self.symm, self.group if self.group is not None else dist.group.WORLD)
+        self._handle = handle
+        elem = self.symm.element_size()
+        peers = _capi.PeerBuffers()
+        for p in range(n):
+            base = handle.buffer_ptrs[p] + handle.offset
+            peers.slots[p] = base
+            peers.flags[p] = base + data * elem
+        self.peers = peers
+        self.row_padded = row_padded
+        self.epoch = 0
+        # Slot views of this rank's buffer: [parity, rank] rows and the merge views.
+        slots = self.symm[:data].view(2, n, row_padded)
+        self.slots = slots
+        handle.barrier()
+        torch.cuda.synchronize(device)
 
     def step(self, q, k_cache, v_cache, *, cu_seqlens_q, seqused_k, max_seqlen_k, block_table,
              k_descale=None, v_descale=None, s_aux=None, softmax_scale=None):
         """One decode step over this rank's slice; returns the merged (out, lse)."""
         from ._attention import attention
         from ._merge import _merge_partials
+        batch, heads, dim = self.shape
+        if self.exchange == "p2p":
+            self.epoch += 1
+            par = self.epoch & 1
+            mine = self.slots[par, self.rank, :self.row]
+            partial, partial_lse = packed_views(mine, batch, heads, dim)
+        else:
+            partial, partial_lse = self.partial, self.partial_lse
         attention(q, k_cache, v_cache, cu_seqlens_q=cu_seqlens_q, seqused_k=seqused_k,
                   max_seqlen_q=1, max_seqlen_k=max_seqlen_k, block_table=block_table,
                   k_descale=k_descale, v_descale=v_descale, softmax_scale=softmax_scale,
-                  s_aux=s_aux if self.rank == 0 else None, out=self.partial, lse=self.partial_lse)
-        dist.all_gather_into_tensor(self.gathered_flat.view(-1), self.packed, group=self.group)
-        return _merge_partials(self.gathered, self.gathered_lse, out=self.out, out_lse=self.out_lse)
+                  s_aux=s_aux if self.rank == 0 else None, out=partial, lse=partial_lse)
+        if self.exchange == "p2p":
+            lib = _capi.library()
+            stream = _capi.stream_of(q.device)
+            row = self.slots[par, self.rank, :self.row_padded]
+            _capi.check(lib.fa_shard_push(_capi.ref(_capi.tensor(row)), _capi.ref(self.peers), self.world,
+                                          self.rank, ctypes.c_uint32(self.epoch), stream))
+            _capi.check(lib.fa_shard_wait(_capi.ref(self.peers), self.world, self.rank,
+                                          ctypes.c_uint32(self.epoch), stream))
+            gathered, gathered_lse = packed_views(self.slots[par, :, :self.row], batch, heads, dim)
+        else:
+            dist.all_gather_into_tensor(self.gathered_flat.view(-1), self.packed, group=self.group)
+            gathered, gathered_lse = self.gathered, self.gathered_lse
+        return _merge_partials(gathered, gathered_lse, out=self.out, out_lse=self.out_lse)

@@ -123,7 +123,8 @@ const char* fa_build_id(void);
 
 /*
  * Pipeline wait time-outs on the current device since the last clear:
- * bit 0 = the tensor-core prefill kernel, bit 1 = the TMA paged-decode kernel.
+ * bit 0 = the tensor-core prefill kernels, bit 1 = the TMA paged-decode
+ * kernel, bit 2 = the sharded-decode exchange (fa_shard_wait).
  * Every mbarrier wait in those kernels gives up after a bounded number of
  * polls, sets its bit and lets the CTA finish, so a stalled pipeline shows
  * up here instead of hanging the GPU; outputs of the affected launch are then
@@ -259,6 +260,38 @@ int fa_merge_attn_states(const fa_tensor* out, const fa_tensor* left, const fa_t
  */
 int fa_merge_partials(const fa_tensor* partial, const fa_tensor* partial_lse,
                       const fa_tensor* out, const fa_tensor* out_lse, void* stream);
+
+/*
+ * KV-sharded decode across GPUs: the exchange of the ranks' partial states over
+ * NVLink peer memory (one process per GPU). Each rank owns a gather buffer
+ * mapped into every rank's address space (symmetric memory): two parities x
+ * world slots of one float32 row [B*Hq*Dv | Hq*B] (a rank's partial output and
+ * LSE), and a flag array of 2*FA_MAX_PEERS uint32 (zero before the first
+ * step). slots[p] / flags[p] are this process's device addresses of rank p's
+ * buffer and flag array. Step epochs start at 1 and grow by 1; step e uses
+ * parity e & 1, and its merge reads this rank's own buffer:
+ *   fa_shard_push: copy this rank's row (already in its own slot `rank` of
+ *     parity e & 1) into slot `rank` of every peer's buffer, then raise
+ *     flags[rank] = e on every peer;
+ *   fa_shard_wait: wait until every peer's flag on this rank reached e (a
+ *     bounded wait: on a timeout bit 2 of fa_pipeline_timeouts is set).
+ * Both are asynchronous on the caller's stream; between them and the merge no
+ * host synchronisation is needed. No counterpart in the reference, which has
+ * no distributed code (flash_attn_mps/vllm.py:5): it replaces an NCCL
+ * all-gather of the partials in front of the N-way merge
+ * (flash_attn_mps/_merge.py:44-57, kernels/merge.metal:30-58).
+ */
+#define FA_MAX_PEERS 8
+
+typedef struct fa_peer_buffers {
+  void* slots[FA_MAX_PEERS];
+  uint32_t* flags[FA_MAX_PEERS];
+} fa_peer_buffers;
+
+int fa_shard_push(const fa_tensor* row, const fa_peer_buffers* peers, int32_t world, int32_t rank,
+                  uint32_t epoch, void* stream);
+
+int fa_shard_wait(const fa_peer_buffers* peers, int32_t world, int32_t rank, uint32_t epoch, void* stream);
 
 #ifdef __cplusplus
 }

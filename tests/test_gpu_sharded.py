@@ -1,4 +1,5 @@
-"""KV-sharded decode over NCCL (``ShardedDecoder``): one spawned process per GPU.
+"""KV-sharded decode (``ShardedDecoder``): one spawned process per GPU, with the
+peer-memory exchange (push + flags + bounded wait) and with the NCCL all-gather.
 
 Each rank holds its ``kv_shard`` slice of every sequence in its own paged cache,
 decodes it, and one all-gather of the packed (out, lse) rows plus the N-way
@@ -37,7 +38,7 @@ def _paged(rows, page, device):
     return cache.to(device), table.to(device), torch.tensor(counts, dtype=torch.int32, device=device)
 
 
-def _worker(rank, world, port, kv, queue):
+def _worker(rank, world, port, kv, exchange, queue):
     import torch.distributed as dist
     from flash_attn_b200.distributed import ShardedDecoder, kv_shard
     from helpers import assert_attention_close, assert_lse_close, reference
@@ -60,11 +61,18 @@ def _worker(rank, world, port, kv, queue):
         kc, table, used = _paged([k[s:e] for k, (s, e) in zip(keys, spans)], 16, device)
         vc, _, _ = _paged([v[s:e] for v, (s, e) in zip(vals, spans)], 16, device)
         cq = torch.arange(B + 1, dtype=torch.int32, device=device)
-        decoder = ShardedDecoder(B, HQ, D, torch.bfloat16, device)
-        for _ in range(2):  # buffers are reused across steps
+        decoder = ShardedDecoder(B, HQ, D, torch.bfloat16, device, exchange=exchange)
+        assert decoder.exchange == exchange
+        results = []
+        for _ in range(3):  # buffers (both parities of the peer-memory exchange) are reused across steps
             out, lse = decoder.step(q, kc, vc, cu_seqlens_q=cq, seqused_k=used,
                                     max_seqlen_k=max(int(used.max()), 1), block_table=table, s_aux=sinks)
+            results.append((out.clone(), lse.clone()))
         torch.cuda.synchronize()
+        from flash_attn_b200 import _capi
+        assert _capi.library().fa_pipeline_timeouts(1) == 0, "an exchange wait timed out"
+        for o, l in results[1:]:
+            assert torch.equal(o, results[0][0]) and torch.equal(l, results[0][1])
         kf, tf, uf = _paged(keys, 16, "cpu")
         vf, _, _ = _paged(vals, 16, "cpu")
         ref, refl = reference(q, kf, vf, cq, used_k=uf, block_table=tf, sinks=sinks)
@@ -77,16 +85,16 @@ def _worker(rank, world, port, kv, queue):
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
 @pytest.mark.parametrize("kv", ["bf16", "fp8"])
-def test_sharded_decoder_matches_full_decode(kv):
+def test_sharded_decoder_matches_full_decode(kv, exchange):
     if torch.cuda.device_count() < 2:
-        pytest.skip("the NCCL all-gather path needs 2 GPUs (one rank per GPU); "
-                    "a single rank would exercise no exchange")
+        pytest.skip("the exchange needs 2 GPUs (one rank per GPU); a single rank would exercise no exchange")
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, kv, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, kv, exchange, queue)) for r in range(world)]
     for p in procs:
         p.start()
     results = [queue.get(timeout=300) for _ in range(world)]
