@@ -16,7 +16,7 @@ with host buffers: H2D of q and of the step's new K/V token, store_kvcache of
 that token, attention, D2H of the output.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload fp8_decode|prefill|prefill_softcap_window|prefill_fp8kv|prefill_alibi|bf16_decode|serving]
+                    [--workload fp8_decode|prefill|prefill_softcap_window|prefill_fp8kv|prefill_alibi|prefill_alibi_softcap|bf16_decode|serving]
                     [--attention-path fused|native] [--small]
 """
 
@@ -1098,7 +1098,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["fp8_decode", "prefill", "prefill_softcap_window", "prefill_fp8kv",
-                                           "prefill_alibi", "bf16_decode", "serving", "store_fp8", "store_bf16",
+                                           "prefill_alibi", "prefill_alibi_softcap", "bf16_decode", "serving", "store_fp8", "store_bf16",
                                            "rope_append", "prefill_d256", "prefill_diffkv", "decode_d256"],
                     default="fp8_decode", help="headline is fp8_decode (config 4); the others run on rank 0 only")
     ap.add_argument("--attention-path", choices=["fused", "native"], default="fused",
@@ -1137,6 +1137,10 @@ def main():
                 return
             elif args.workload == "prefill_alibi":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, alibi=True)
+                value, unit = r["TFLOP/s"], "TFLOP/s"
+            elif args.workload == "prefill_alibi_softcap":
+                r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, alibi=True,
+                                softcap=50.0)
                 value, unit = r["TFLOP/s"], "TFLOP/s"
             elif args.workload == "prefill_fp8kv":
                 r = run_prefill(peaks, peak_kind, steps=args.steps, warmup=args.warmup, small=args.small, fp8_kv=True)

@@ -145,14 +145,17 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
 }
 
 // HDIM: head dim (64 or 128) = number of 64-element swizzle regions x 64.
-// ALIBI: scores minus slope * |q_abs - key| (not combined with a softcap).
+// ALIBI: scores minus slope * |q_abs - key|; with SOFTCAP as well, the
+// softcapped score minus the bias (the softcap then runs before the row max).
 template <bool BF16, bool SOFTCAP, int HDIM, bool ALIBI>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_sm100_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
                          const PrefillParams p) {
   static_assert(HDIM == 64 || HDIM == 128, "head dim");
-  static_assert(!(SOFTCAP && ALIBI), "softcap with ALiBi runs on the mma.sync kernel");
+  // Softcap in the exponential stage (its max commutes with tanh); with ALiBi
+  // the capped and biased scores are formed before the row max instead.
+  constexpr bool CAP_IN_EXP = SOFTCAP && !ALIBI;
   constexpr int kHalves = HDIM / 64;             // 64-element regions per row
   constexpr int kLoadBytes = kHalves * kRegion;      // bytes of one Q tile actually loaded
   constexpr int kKVLoadBytes = kHalves * kKVRegion;  // bytes of one K/V tile actually loaded
@@ -454,12 +457,47 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32_at<96>(tS + 96, r);
         }
         tmem_wait_ld();
-        if (need_mask) {
+        if (!(ALIBI && SOFTCAP) && need_mask) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
             if (i < c_lo || i > c_hi) r[i] = __float_as_uint(-INFINITY);
         }
-        if constexpr (ALIBI) {
+        if constexpr (ALIBI && SOFTCAP) {
+          // v = cap*log2e*tanh(s*scale/cap) - slope*log2e*|q_abs - key| (the
+          // reference's capped score minus the ALiBi bias, in log2 units), with
+          // tanh(y) = 1 - 2/(e^(2y)+1) as in the softcap-only stage below, in
+          // two in-place passes over the row; then the mask.
+          const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
+          {
+            const Exp2Poly<false> tanh_poly;
+#pragma unroll
+            for (int i = 0; i < BN; i += 2) {
+              float u0, u1, e0, e1;
+              f2unpack(fmul2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), tanh_k2), u0, u1);
+              tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
+              r[i] = __float_as_uint(e0);
+              r[i + 1] = __float_as_uint(e1);
+            }
+          }
+          const float base = (float)(q_abs - key0);
+          const uint64_t nslope2 = f2pack(-slope_l2, -slope_l2), cap_l2x2 = f2pack(cap_l2, cap_l2);
+          const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f);
+#pragma unroll
+          for (int i = 0; i < BN; i += 2) {
+            float d0, d1, v0, v1;
+            f2unpack(fadd2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), one2), d0, d1);
+            const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
+            const uint64_t dist2 = f2pack(fabsf(base - (float)i), fabsf(base - (float)(i + 1)));
+            f2unpack(ffma2(t2, cap_l2x2, fmul2(dist2, nslope2)), v0, v1);
+            r[i] = __float_as_uint(v0);
+            r[i + 1] = __float_as_uint(v1);
+          }
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < BN; ++i)
+              if (i < c_lo || i > c_hi) r[i] = __float_as_uint(-INFINITY);
+          }
+        } else if constexpr (ALIBI) {
           // v = s*scale*log2e - slope*log2e*|q_abs - key| (the reference's
           // score minus the ALiBi bias, in log2 units); masked scores stay -inf.
           const float base = (float)(q_abs - key0);
@@ -484,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         // scale > 0 and tanh is increasing: the max commutes with both.
-        const float m_tile = SOFTCAP ? (mx == -INFINITY ? -INFINITY : cap_l2 * tanh_id(mx * cap_in)) : mx * sl2e;
+        const float m_tile = CAP_IN_EXP ? (mx == -INFINITY ? -INFINITY : cap_l2 * tanh_id(mx * cap_in)) : mx * sl2e;
         float factor = 1.f;
         if (m_tile > m_run + kRescaleThreshold || (m_run == -INFINITY && m_tile != -INFINITY)) {
           factor = m_run == -INFINITY ? 0.f : ex2(m_run - m_tile);
@@ -511,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 8; ++i) {
             float p0, p1;
             const float s0 = __uint_as_float(r[c8 * 16 + 2 * i]), s1 = __uint_as_float(r[c8 * 16 + 2 * i + 1]);
-            if constexpr (SOFTCAP) {
+            if constexpr (CAP_IN_EXP) {
               // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1):
               // e^(2y) on the FMA pipe (degree-4 polynomial, argument clamped
               // to +-64 where tanh is +-1 in fp32), one MUFU rcp, one MUFU ex2.
@@ -690,7 +728,6 @@ int prefill_sm100_supported(const AttnParams& p) {
       if (v <= 0 || (v * 2) % 16 != 0) return 0;
   }
   if (p.mask || p.leftpad || p.cp_n > 1) return 0;
-  if (p.alibi && p.softcap > 0.f) return 0;  // softcap + ALiBi: mma.sync kernel
   if (p.sinks && !(p.sink_t == FA_F32 || p.sink_t == FA_F16 || p.sink_t == FA_BF16)) return 0;
   if (p.qs2 != 1 || p.ks3 != 1 || p.vs3 != 1 || p.os2 != 1) return 0;
   if (!al16(p.q) || !al16(p.k) || !al16(p.v) || !al16(p.out)) return 0;
@@ -772,9 +809,9 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   auto pick = [&](auto hd) {
     constexpr int H = decltype(hd)::value;
     if (p.qt == FA_BF16)
-      return cap ? prefill_sm100_kernel<true, true, H, false>
+      return cap ? (alibi ? prefill_sm100_kernel<true, true, H, true> : prefill_sm100_kernel<true, true, H, false>)
                  : alibi ? prefill_sm100_kernel<true, false, H, true> : prefill_sm100_kernel<true, false, H, false>;
-    return cap ? prefill_sm100_kernel<false, true, H, false>
+    return cap ? (alibi ? prefill_sm100_kernel<false, true, H, true> : prefill_sm100_kernel<false, true, H, false>)
                : alibi ? prefill_sm100_kernel<false, false, H, true> : prefill_sm100_kernel<false, false, H, false>;
   };
   auto kernel = p.DQ <= 64 ? pick(std::integral_constant<int, 64>{}) : pick(std::integral_constant<int, 128>{});

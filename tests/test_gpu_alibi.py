@@ -1,8 +1,9 @@
 """ALiBi prefill on the tcgen05 kernel against the oracle: scores minus
 slope * |q_abs - key| (lower-right aligned), bf16/f16, head dims 64/128,
 causal and not, per-head [H] and per-request [B, H] slopes, windows and sinks,
-a paged vLLM call over an FP8 E4M3 cache, and single-query ALiBi decode (which
-keeps the split-KV kernels)."""
+ALiBi together with a softcap (the capped score minus the bias, reference
+kernels/attention.metal:47-51), a paged vLLM call over an FP8 E4M3 cache, and
+single-query ALiBi decode (which keeps the split-KV kernels)."""
 
 import pytest
 import torch
@@ -30,6 +31,37 @@ def test_alibi_prefill(device, dtype, dim, causal):
     ref, refl = reference(q, k, v, cq, ck, causal=causal, alibi=slopes)
     assert_attention_close(out, ref, dtype)
     assert_lse_close(lse, refl)
+
+
+def _kernel_names(fn):
+    """Names of the CUDA kernels ``fn`` launches (empty if the profiler sees none)."""
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.key for e in prof.key_averages() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dim", [128, 64])
+@pytest.mark.parametrize("causal", [True, False])
+def test_alibi_with_softcap_prefill(device, dtype, dim, causal):
+    g = torch.Generator().manual_seed(95)
+    qlens, klens = [300, 1, 129, 520], [300, 70, 400, 520]
+    q = (3 * torch.randn(sum(qlens), 8, dim, generator=g)).to(dtype).to(device)
+    k = torch.randn(sum(klens), 2, dim, generator=g).to(dtype).to(device)
+    v = torch.randn(sum(klens), 2, dim, generator=g).to(dtype).to(device)
+    cq, ck = cu(qlens, device), cu(klens, device)
+    slopes = torch.tensor([2.0 ** (-(i + 1)) for i in range(8)], device=device)
+    sinks = torch.linspace(-1, 1, 8, device=device)
+    run = lambda: vllm_attention(q, k, v, max(qlens), cq, max(klens), cu_seqlens_k=ck, causal=causal, softcap=6.0,
+                                 alibi_slopes=slopes, s_aux=sinks, return_softmax_lse=True)
+    out, lse = run()
+    ref, refl = reference(q, k, v, cq, ck, causal=causal, softcap=6.0, alibi=slopes, sinks=sinks)
+    assert_attention_close(out, ref, dtype)
+    assert_lse_close(lse, refl)
+    names = _kernel_names(run)
+    if names:  # the combination runs on the tensor-core prefill, not the mma.sync fallback
+        assert any("prefill_sm100_kernel" in n for n in names), names
 
 
 def test_alibi_per_request_slopes_window_sinks(device):
