@@ -270,7 +270,7 @@ inline bool al16(const void* ptr) { return ((uintptr_t)ptr & 15u) == 0; }
 
 // Wide head dims (prefill_wide_sm100.cu): QK head dim 129..256, V head dim up
 // to 256, one query tile per CTA. prefill_wide_dims: the head dims are in its
-// range; prefill_wide_supported: also the layout (packed K/V, no ALiBi).
+// range; prefill_wide_supported: also the features (no ALiBi).
 bool prefill_wide_dims(const AttnParams& p);
 int prefill_wide_supported(const AttnParams& p);
 int launch_prefill_wide(const AttnParams& p, const pf::PrefillParams& pp, cudaStream_t stream);

@@ -714,7 +714,7 @@ int prefill_sm100_supported(const AttnParams& p) {
   // padded columns on loads (adding nothing to Q K^T; V's give O columns that
   // are never stored) and clips them on the tile stores.
   // Head dims above 128 (QK up to 256, V up to 256): the one-tile kernel of
-  // prefill_wide_sm100.cu, packed K/V without ALiBi.
+  // prefill_wide_sm100.cu, packed or paged K/V without ALiBi.
   const bool wide = prefill_wide_dims(p);
   if (wide && !prefill_wide_supported(p)) return 0;
   if (!wide && (p.DQ != p.DV || p.DQ < 8 || p.DQ > 128 || p.DQ % 8)) return 0;

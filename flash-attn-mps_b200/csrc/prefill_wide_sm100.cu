@@ -108,6 +108,38 @@ __device__ __forceinline__ Item make_wide_item(const PrefillParams& p, int w) {
   return it;
 }
 
+// One BN-key tile of R 64-column regions into dst. Packed K/V: one 3-D box per
+// region. Paged K/V: the keys arrive as page boxes (box_rows tokens x 64 head
+// dims each, spread over the warp's lanes) through block_table; pages past the
+// sequence or the table use page -1, which TMA fills with zeros. Called by the
+// whole warp; lane 0 arms the barrier first.
+template <int R>
+__device__ __forceinline__ void load_kv_tile(const PrefillParams& p, const Item& it, const CUtensorMap* map,
+                                             uint32_t dst, uint32_t full_bar, int key0, int lane) {
+  if (p.table == nullptr) {
+    if (lane == 0) {
+      mbar_expect_tx(full_bar, R * kKVRegion);
+#pragma unroll
+      for (int r = 0; r < R; ++r) tma_load_3d(dst + r * kKVRegion, map, full_bar, r * 64, it.kh, it.k_begin + key0);
+    }
+    __syncwarp();
+    return;
+  }
+  const int nb = BN / p.box_rows;
+  if (lane == 0) mbar_expect_tx(full_bar, R * kKVRegion);
+  __syncwarp();
+  for (int bx = lane; bx < R * nb; bx += 32) {
+    const int r = bx / nb, c = bx - r * nb;
+    const int pos = key0 + c * p.box_rows;
+    const int pg = pos >> p.page_shift;
+    int blk = -1;
+    if (pos < it.k_len && pg < p.bt_cols) blk = __ldg(p.table + (int64_t)it.b * p.bt0 + (int64_t)pg * p.bt1);
+    tma_load_4d(dst + r * kKVRegion + c * p.box_rows * 128, map, full_bar, r * 64, it.kh,
+                pos & ((1 << p.page_shift) - 1), blk);
+  }
+  __syncwarp();
+}
+
 // DQK / DV: padded QK and V head dims (multiples of 64); the tensor maps
 // carry the true dims, so padded columns load as zeros and are never stored.
 template <bool BF16, bool SOFTCAP, int DQK, int DV>
@@ -200,14 +232,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
       ++qloads;
       for (int t = 0; t < it.n_all; ++t) {
         if (kloads > 0 && !(ok = wwait(bar(W_KE), (kloads - 1) & 1))) break;
-        if (lane == 0) {
-          const int row = it.k_begin + (it.j_first + t) * BN;
-          mbar_expect_tx(bar(W_KF), RQ * kKVRegion);
-#pragma unroll
-          for (int r = 0; r < RQ; ++r)
-            tma_load_3d(base + L::OFF_K + r * kKVRegion, &tk, bar(W_KF), r * 64, it.kh, row);
-        }
-        __syncwarp();
+        load_kv_tile<RQ>(p, it, &tk, base + L::OFF_K, bar(W_KF), (it.j_first + t) * BN, lane);
         ++kloads;
       }
     }
@@ -225,14 +250,7 @@ __global__ void __launch_bounds__(kWThreads, 1)
       if (w < 0) break;
       for (int t = 0; t < it.n_all; ++t) {
         if (vloads > 0 && !(ok = wwait(bar(W_VE), (vloads - 1) & 1))) break;
-        if (lane == 0) {
-          const int row = it.k_begin + (it.j_first + t) * BN;
-          mbar_expect_tx(bar(W_VF), RV * kKVRegion);
-#pragma unroll
-          for (int r = 0; r < RV; ++r)
-            tma_load_3d(base + L::OFF_V + r * kKVRegion, &tv, bar(W_VF), r * 64, it.kh, row);
-        }
-        __syncwarp();
+        load_kv_tile<RV>(p, it, &tv, base + L::OFF_V, bar(W_VF), (it.j_first + t) * BN, lane);
         ++vloads;
       }
     }
@@ -534,15 +552,15 @@ void* pick_wide(bool bf16, bool cap) {
 }  // namespace
 
 // QK head dims 129..256 and V head dims up to 256, multiples of 8 (16-byte
-// rows), packed K/V, no ALiBi; the other conditions are those of the two-tile
-// kernel (checked by the caller).
+// rows), packed or paged K/V, no ALiBi; the other conditions (page sizes,
+// strides, alignment) are those of the two-tile kernel (checked by the caller).
 bool prefill_wide_dims(const AttnParams& p) {
   return p.DQ > 128 && p.DQ <= 256 && p.DV >= 8 && p.DV <= 256 && p.DQ % 8 == 0 && p.DV % 8 == 0;
 }
 
 int prefill_wide_supported(const AttnParams& p) {
   if (!prefill_wide_dims(p)) return 0;
-  if (p.paged || p.alibi) return 0;
+  if (p.alibi) return 0;
   return 1;
 }
 
@@ -560,9 +578,15 @@ int launch_prefill_wide(const AttnParams& p, const PrefillParams& pp_in, cudaStr
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, p.q, p.qt, p.DQ, p.T, p.HQ, p.qs0, p.qs1);
   if (rc) return rc;
-  rc = make_map(&mk, p.k, p.kt, p.DQ, p.k_rows, p.HK, p.ks1, p.ks2, BN);
-  if (rc) return rc;
-  rc = make_map(&mv, p.v, p.vt, p.DV, p.k_rows, p.HK, p.vs1, p.vs2, BN);
+  if (p.paged) {
+    rc = make_page_map(&mk, p.k, p.kt, p.DQ, p.HK, p.page, p.k_pages, p.ks0, p.ks1, p.ks2, pp_in.box_rows);
+    if (rc) return rc;
+    rc = make_page_map(&mv, p.v, p.vt, p.DV, p.HK, p.page, p.k_pages, p.vs0, p.vs1, p.vs2, pp_in.box_rows);
+  } else {
+    rc = make_map(&mk, p.k, p.kt, p.DQ, p.k_rows, p.HK, p.ks1, p.ks2, BN);
+    if (rc) return rc;
+    rc = make_map(&mv, p.v, p.vt, p.DV, p.k_rows, p.HK, p.vs1, p.vs2, BN);
+  }
   if (rc) return rc;
   PrefillParams pp = pp_in;
   pp.n_pairs = (p.max_q + BM - 1) / BM;

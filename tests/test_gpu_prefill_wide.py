@@ -7,7 +7,8 @@ is checked against the float64 oracle (reference tests/reference.py:6-90)
 with the reference's tolerances (max-abs 1e-2 on 16-bit outputs, LSE 1e-3):
 several key tiles, causal and not, q_len != k_len, GQA, windows, softcap,
 sinks, descales, padded dims, FP8 K/V (exact 16-bit copy in front of the
-kernel) and the batch-invariant mode.
+kernel), paged caches (pages of 16..256 tokens through a permuted block table)
+and the batch-invariant mode.
 """
 
 import pytest
@@ -109,3 +110,49 @@ def test_wide_batch_invariant_mode_is_bitwise_stable(device):
     assert torch.equal(full[qlens[0]:qlens[0] + qlens[1]], alone)
     ref, _ = reference(q, k, v, cq, ck, causal=True)
     assert_attention_close(full, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("page", [16, 32, 64, 256])
+@pytest.mark.parametrize("dims", [(256, 256), (192, 128)])
+def test_wide_paged_cache_against_oracle(device, page, dims):
+    # vLLM prefill over a paged cache (permuted pages, K and V as views of one
+    # packed allocation): page boxes gathered through the block table, pages
+    # past each sequence zero-filled, NaN in the unused tail slots.
+    dq, dv = dims
+    g = torch.Generator().manual_seed(16 + page)
+    qlens, klens = [150, 64, 1], [700, 300, 129]
+    cols = max(klens) // page + 1
+    packed = torch.randn(3 * cols, page, 2, dq + dv, generator=g).to(torch.bfloat16).to(device)
+    kc, vc = packed.split([dq, dv], dim=-1)
+    table = torch.randperm(3 * cols, generator=g).int().reshape(3, cols).to(device)
+    for b, n in enumerate(klens):
+        last = table[b, n // page].item()
+        packed[last, n % page:] = float("nan")
+    q = torch.randn(sum(qlens), 8, dq, generator=g).to(torch.bfloat16).to(device)
+    cq = cu(qlens, device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    out, lse = vllm_varlen(q, kc, vc, max(qlens), cq, max(klens), seqused_k=used, block_table=table,
+                           causal=True, return_softmax_lse=True)
+    ref, refl = reference(q, kc, vc, cq, used_k=used, block_table=table, causal=True)
+    assert torch.isfinite(out).all()
+    assert_attention_close(out, ref, torch.bfloat16)
+    assert_lse_close(lse, refl)
+
+
+def test_wide_paged_softcap_window_sinks(device):
+    g = torch.Generator().manual_seed(17)
+    qlens, klens, page = [200, 77], [520, 900], 16
+    cols = max(klens) // page + 1
+    kc = torch.randn(2 * cols, page, 4, 256, generator=g).to(torch.float16).to(device)
+    vc = torch.randn(2 * cols, page, 4, 256, generator=g).to(torch.float16).to(device)
+    table = torch.randperm(2 * cols, generator=g).int().reshape(2, cols).to(device)
+    q = (2 * torch.randn(sum(qlens), 8, 256, generator=g)).to(torch.float16).to(device)
+    cq = cu(qlens, device)
+    used = torch.tensor(klens, dtype=torch.int32, device=device)
+    sinks = torch.linspace(-1, 1, 8, device=device)
+    out, lse = vllm_varlen(q, kc, vc, max(qlens), cq, max(klens), seqused_k=used, block_table=table,
+                           causal=True, window_size=[300, 0], softcap=30.0, s_aux=sinks, return_softmax_lse=True)
+    ref, refl = reference(q, kc, vc, cq, used_k=used, block_table=table, causal=True, window=(300, 0),
+                          softcap=30.0, sinks=sinks)
+    assert_attention_close(out, ref, torch.float16)
+    assert_lse_close(lse, refl)
