@@ -634,7 +634,20 @@ def run_prefill(peaks, peak_kind, steps=20, warmup=5, softcap=0.0, window=(-1, -
                         + (" (small profiling case)" if small else ""),
             "total_tokens": total, "tflop_per_step": flops / 1e12, "ms_per_step": ms, "steps": steps,
             "TFLOP/s": tflops,
-            "roofline": roofline_tensor(tflops, peaks, peak_kind, sustained)}
+            "roofline": dict(roofline_tensor(tflops, peaks, peak_kind, sustained), **prefill_traffic(
+                plain=not (softcap or window[0] >= 0 or fp8_kv or kv_slice or alibi or dims or small),
+                tokens=total, cfg=cfg, dims=(dq, dv)))}
+
+
+def prefill_traffic(plain, tokens, cfg, dims):
+    """DRAM bytes of one config-2 prefill launch from the ncu capture in
+    profiles/ (plain config-2 workload only), beside the algorithmic bytes:
+    Q, K and V read once, the output and the LSE written once."""
+    dq, dv = dims
+    alg = tokens * (cfg["hq"] * dq * 2 + cfg["hkv"] * (dq + dv) * 2 + cfg["hq"] * dv * 2 + cfg["hq"] * 4)
+    traffic = profiled_traffic("prefill_sm100_cfg2_traffic.md") if plain else None
+    return {"traffic": traffic, "algorithmic_bytes": alg,
+            "traffic_source": "profiles/prefill_sm100_cfg2_traffic.md (ncu, full launch)" if traffic else None}
 
 
 def roofline_tensor(tflops, peaks, peak_kind, sustained=False):

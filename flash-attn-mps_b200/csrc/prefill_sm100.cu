@@ -65,6 +65,7 @@ constexpr int kThreads = 384;                 // 2 softmax warpgroups + (TMA, MM
 // softmax warpgroups take them, so that each softmax thread holds its whole
 // 128-column S row. 8 warps x 208 + 4 warps x 88 = 12 warps x 168.
 constexpr int kLaunchRegs = 168;
+
 #ifndef FAB_PF_SM_REGS
 #define FAB_PF_SM_REGS 208
 #endif
@@ -111,12 +112,19 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {  // f
 __device__ __forceinline__ Item make_item(const PrefillParams& p, int w) {
   Item it;
   const int hsteps = p.HQ >> p.head_pairs;  // query heads, or head pairs
-  const int per = hsteps * p.B;
-  const int pair = p.n_pairs - 1 - w / per;
-  const int rem = w - (w / per) * per;
+  // Work order: groups of group_reqs requests, whose K/V stay in L2 while the
+  // CTAs work through them; within a group row blocks heaviest first, then
+  // head (pair), then request.
+  const int per_group = p.n_pairs * hsteps * p.group_reqs;
+  const int g = w / per_group;
+  const int local = w - g * per_group;
+  const int b0 = g * p.group_reqs;
+  const int per = hsteps * min(p.group_reqs, p.B - b0);
+  const int pair = p.n_pairs - 1 - local / per;
+  const int rem = local - (local / per) * per;
   it.h = (rem % hsteps) << p.head_pairs;
   it.h_b = it.h + p.head_pairs;
-  it.b = rem / hsteps;
+  it.b = b0 + rem / hsteps;
   it.q_begin = p.cu_q[it.b * p.cq0];
   it.q_len = p.cu_q[(it.b + 1) * p.cq0] - it.q_begin;
   it.row_a = pair * (p.head_pairs ? BM : 2 * BM);
@@ -776,6 +784,7 @@ int launch_prefill_sm100(const AttnParams& p, cudaStream_t stream) {
   // Pair query heads h, h+1 (same KV head) when the heads per KV head are even.
   pp.head_pairs = (p.HQ / p.HK) % 2 == 0 ? 1 : 0;
   pp.n_pairs = pp.head_pairs ? (p.max_q + BM - 1) / BM : (p.max_q + 2 * BM - 1) / (2 * BM);
+  pp.group_reqs = prefill_group_reqs(p);
   pp.causal = p.causal;
   pp.causal_b = p.dynamic ? p.causal_b : nullptr; pp.ca0 = p.ca0;
   pp.sinks = p.sinks; pp.sink_t = p.sink_t; pp.si0 = p.si0;

@@ -74,17 +74,22 @@ __device__ __forceinline__ bool wwait(uint32_t bar, uint32_t parity) {
   return warp_wait_flag(bar, parity, &g_prefill_wide_timeout);
 }
 
-// One 128-row query block of one (request, query head). Items are ordered by
-// block index descending (the costliest causal blocks first), then head,
-// then request. Tile B of the record is unused.
+// One 128-row query block of one (request, query head). Items come in groups
+// of group_reqs requests (whose K/V stay in L2 together); within a group by
+// block index descending (the costliest causal blocks first), then head, then
+// request. Tile B of the record is unused.
 __device__ __forceinline__ Item make_wide_item(const PrefillParams& p, int w) {
   Item it;
-  const int per = p.HQ * p.B;
-  const int blk = p.n_pairs - 1 - w / per;
-  const int rem = w - (w / per) * per;
+  const int per_group = p.n_pairs * p.HQ * p.group_reqs;
+  const int g = w / per_group;
+  const int local = w - g * per_group;
+  const int b0 = g * p.group_reqs;
+  const int per = p.HQ * min(p.group_reqs, p.B - b0);
+  const int blk = p.n_pairs - 1 - local / per;
+  const int rem = local - (local / per) * per;
   it.h = rem % p.HQ;
   it.h_b = it.h;
-  it.b = rem / p.HQ;
+  it.b = b0 + rem / p.HQ;
   it.q_begin = p.cu_q[it.b * p.cq0];
   it.q_len = p.cu_q[(it.b + 1) * p.cq0] - it.q_begin;
   it.row_a = blk * BM;
