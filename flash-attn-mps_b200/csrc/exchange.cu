@@ -15,7 +15,8 @@
 //   4. the N-way merge kernel combines the N slots of parity e & 1.
 // Two parities make the buffer safe to reuse: a rank can start step e+1 only
 // after every peer has pushed step e, so no rank is ever more than one step
-// ahead of another's reads. No TMA, no multicast: plain peer stores and loads.
+// ahead of another's reads. No TMA and no NVSwitch reductions: plain peer
+// stores and loads.
 // A wait that gives up sets g_exchange_timeout (fa_pipeline_timeouts bit 2)
 // and returns; the merged outputs of that step are then undefined.
 #include <algorithm>

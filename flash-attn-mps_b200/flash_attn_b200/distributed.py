@@ -94,8 +94,8 @@ class ShardedDecoder:
             self.gathered, self.gathered_lse = packed_views(self.gathered_flat, batch, q_heads, head_dim)
 
     def _init_p2p(self, device):
-        # Plain peer loads and stores only: the buffer needs no NVLink
-        # multicast object.
+        # Plain peer loads and stores only: no NVSwitch-side object is bound
+        # to the buffer.
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
         n, row = self.world, self.row
