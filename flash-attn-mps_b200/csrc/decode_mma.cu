@@ -613,8 +613,9 @@ template <typename MT, bool FP8, int D, int NH, bool PREC, bool QFOLD>
 int launch_cfg(const AttnParams& p, int splits, int span, cudaStream_t stream) {
   constexpr int W = FP8 ? FAB_DECODE_FP8_W : FAB_DECODE_16_W;
   constexpr int NST = FP8 ? FAB_DECODE_FP8_NST : FAB_DECODE_16_NST;
-  // 256-wide rows: a 3-stage ring of 32 KB stages leaves room for 2 CTAs per SM.
-  constexpr int MINB = D > 128 ? 2 : (FP8 && NH == 16) ? 1 : (FP8 ? FAB_DECODE_FP8_MINB : FAB_DECODE_16_MINB);
+  // 256-wide rows: a 3-stage ring of 32 KB stages leaves room for 2 CTAs per
+  // SM (FP8 with 16 heads per CTA: one, its accumulators need the registers).
+  constexpr int MINB = (FP8 && NH == 16) ? 1 : D > 128 ? 2 : (FP8 ? FAB_DECODE_FP8_MINB : FAB_DECODE_16_MINB);
   constexpr int smem = smem_bytes<FP8, D, W, NH>(NST);
   const int shift = page_shift_of(p);
   const bool tma = use_tma(p, shift);
@@ -675,11 +676,11 @@ int decode_mma_supported(const AttnParams& p) {
   if (!fp8 && p.kt != p.qt) return 0;
   if (p.DQ != p.DV) return 0;
   // Head dims up to 128 (multiples of 8, of 16 for FP8 rows) run on the 64-
-  // or 128-wide instantiation, 16-bit head dims 129..256 on the 256-wide one:
-  // the tail of Q reads as zero, K/V chunks past the true dim are zero-filled
-  // (TMA out-of-bounds fill or cp.async zero fill) and only true-dim outputs
-  // are written.
-  if (p.DQ < 8 || p.DQ > (fp8 ? 128 : 256) || p.DQ % (fp8 ? 16 : 8)) return 0;
+  // (16-bit) or 128-wide instantiation, head dims 129..256 on the 256-wide
+  // one: the tail of Q reads as zero, K/V chunks past the true dim are
+  // zero-filled (TMA out-of-bounds fill or cp.async zero fill) and only
+  // true-dim outputs are written.
+  if (p.DQ < 8 || p.DQ > 256 || p.DQ % (fp8 ? 16 : 8)) return 0;
   if (p.alibi || p.mask != 0) return 0;
   if (p.ks3 != 1 || p.vs3 != 1) return 0;
   const int elt = fp8 ? 1 : 2;
@@ -736,7 +737,8 @@ int launch_decode_mma(const AttnParams& p, int splits, int span, cudaStream_t st
   const bool prec = p.ot == FA_F32;
   if (fp8) {
     const bool qfold = p.qt == FA_BF16;
-    return launch_heads<__half, true, 128>(p, splits, span, prec, qfold, stream);
+    return p.DQ <= 128 ? launch_heads<__half, true, 128>(p, splits, span, prec, qfold, stream)
+                       : launch_heads<__half, true, 256>(p, splits, span, prec, qfold, stream);
   }
   if (p.qt == FA_BF16) {
     return p.DQ <= 64    ? launch_heads<__nv_bfloat16, false, 64>(p, splits, span, prec, false, stream)
