@@ -6,12 +6,13 @@ paged cache (``kv_shard``). A decode step is:
 1. local split-KV decode over the rank's slice into an fp32 partial
    ``(out [B,Hq,Dv], lse [Hq,B])`` -- the tensor-core decode kernel plus its
    split merge -- written as one flat fp32 row (out first, then lse);
-2. the exchange of the rows: by default one NCCL all-gather of the rows over
-   NVLink / NVSwitch; or (``exchange="p2p"``) over peer memory: the row is
-   decoded straight into this rank's slot of a gather buffer in symmetric
-   memory, the push kernel copies it into the same slot of every peer's buffer
-   and raises a per-rank flag there, and a one-warp kernel waits (bounded)
-   for every peer's flag (``fa_shard_push`` / ``fa_shard_wait``);
+2. the exchange of the rows: by default over peer memory (``exchange="p2p"``):
+   the row is decoded straight into this rank's slot of a gather buffer in
+   symmetric memory, the push kernel copies it into the same slot of every
+   peer's buffer and raises a per-rank flag there, and a one-warp kernel waits
+   (bounded) for every peer's flag (``fa_shard_push`` / ``fa_shard_wait``);
+   or (``exchange="nccl"``) one NCCL all-gather of the rows over NVLink /
+   NVSwitch;
 3. the N-way LSE merge kernel (the same one that combines split-KV partials)
    reads the gathered rows through strides and writes the final output in the
    caller's dtype on every rank.
@@ -29,6 +30,15 @@ import torch
 import torch.distributed as dist
 
 from . import _capi
+
+
+def _symmetric_memory_available():
+    """torch's symmetric memory (the peer-memory exchange's buffer) is importable."""
+    try:
+        import torch.distributed._symmetric_memory  # noqa: F401
+    except ImportError:
+        return False
+    return True
 
 
 def kv_shard(length, rank, world):
@@ -62,13 +72,15 @@ def gather_partials(partial_out, partial_lse, group=None):
 class ShardedDecoder:
     """Reusable buffers for KV-sharded decode steps of a fixed batch shape.
 
-    ``exchange="nccl"`` (the default; ``FAB_SHARD_EXCHANGE`` overrides it): the
-    row is all-gathered with NCCL into ``[N, row]``.
-    ``exchange="p2p"`` (CUDA devices, ``world > 1``): a gather buffer in
-    symmetric memory -- two parities x N slots of the packed row
-    ``[B*Hq*Dv | Hq*B]`` plus a flag array -- mapped into every rank; step e
-    decodes into this rank's slot of parity e & 1, pushes it to every peer over
-    NVLink and waits for the peers' flags before the merge.
+    ``exchange="p2p"`` (the default on CUDA devices with ``world > 1``;
+    ``FAB_SHARD_EXCHANGE`` overrides it): a gather buffer in symmetric memory
+    -- two parities x N slots of the packed row ``[B*Hq*Dv | Hq*B]`` plus a
+    flag array -- mapped into every rank; step e decodes into this rank's slot
+    of parity e & 1, pushes it to every peer over NVLink and waits for the
+    peers' flags before the merge (8 ranks, config 4: 0.439 ms per step
+    against 0.459 with the NCCL all-gather).
+    ``exchange="nccl"`` (and every CPU / single-rank group): the row is
+    all-gathered with NCCL (or gloo) into ``[N, row]``.
     The merge reads the gathered out/lse parts as strided views either way.
     """
 
@@ -81,8 +93,8 @@ class ShardedDecoder:
         self.out = torch.empty(batch, q_heads, head_dim, dtype=out_dtype, device=device)
         self.out_lse = torch.empty(q_heads, batch, dtype=torch.float32, device=device)
         if exchange is None:
-            exchange = os.environ.get("FAB_SHARD_EXCHANGE", "nccl")
-        if self.world < 2 or torch.device(device).type != "cuda":
+            exchange = os.environ.get("FAB_SHARD_EXCHANGE", "p2p")
+        if self.world < 2 or torch.device(device).type != "cuda" or not _symmetric_memory_available():
             exchange = "nccl"
         self.exchange = exchange
         if exchange == "p2p":
