@@ -176,6 +176,65 @@ __device__ __forceinline__ float tanh_id(float y) {
   return fmaf(-2.f, rcp(1.f + ex2(y * 2.8853900817779268f)), 1.f);
 }
 
+// Softcap on the FMA pipe for bounded arguments: tanh(y) = y * Q(y^2) on
+// |y| <= 3/4, Q a degree-4 minimax polynomial in y^2 with Q(0) = 1 (Remez fit,
+// relative error 6.5e-7; float32 Horner 7.4e-7 relative, 4.6e-7 absolute --
+// below the identity route's ~1.5e-6; flash-attn-mps_b200/csrc/fit_tanh_poly.py).
+// With y = s * c (c = scale / cap) and cap * log2e * c = scale * log2e = sl2,
+//   cap * log2e * tanh(s * c) = s * sl2 * Q(y^2):
+// the score scale folds into Q's coefficients (y itself is formed first, so
+// no coefficient depends on the cap and none can under- or overflow for an
+// extreme cap). Two packed multiplies, four packed FMAs and the caller's
+// final FMA per pair of scores, no MUFU operation.
+constexpr float kSoftcapPolyY = 0.75f;
+struct TanhPoly {
+  uint64_t c2, k0, k1, k2, k3, k4;
+  __device__ __forceinline__ TanhPoly(float sl2, float c) {
+    c2 = f2pack(c, c);
+    k0 = f2pack(sl2, sl2);
+    const float a1 = sl2 * -3.332966864e-01f, a2 = sl2 * 1.326823682e-01f;
+    const float a3 = sl2 * -5.027795583e-02f, a4 = sl2 * 1.310583670e-02f;
+    k1 = f2pack(a1, a1);
+    k2 = f2pack(a2, a2);
+    k3 = f2pack(a3, a3);
+    k4 = f2pack(a4, a4);
+  }
+  // cap * log2e * tanh(s * c) + add, for a pair of scores s.
+  __device__ __forceinline__ uint64_t fma(uint64_t s2, uint64_t add2) const {
+    const uint64_t y = fmul2(s2, c2);
+    const uint64_t v = fmul2(y, y);
+    uint64_t q = ffma2(k4, v, k3);
+    q = ffma2(q, v, k2);
+    q = ffma2(q, v, k1);
+    q = ffma2(q, v, k0);
+    return ffma2(s2, q, add2);
+  }
+};
+
+// Largest |s| for which TanhPoly applies (|s * c| <= 3/4), for a positive
+// finite c = scale / cap only (else -1: never). With c > 0 (and so every
+// k_i's sign that of Q's coefficient) a masked score s = -inf gives y = -inf,
+// v = +inf, Q = +inf (leading coefficient > 0) and s * sl2 * Q = -inf exactly,
+// so 2^(logit - m) is exactly 0 without a select.
+__device__ __forceinline__ float softcap_poly_limit(float c) {
+  return (c > 0.f && c < INFINITY) ? kSoftcapPolyY / c : -1.f;
+}
+
+// Largest |s| of a score row, as 8 independent 3-input max chains (a NaN
+// score, which only non-finite inputs produce, is ignored; an infinite one
+// makes the bound infinite).
+template <int N>
+__device__ __forceinline__ float row_absmax(const uint32_t (&r)[N]) {
+  float am8[8];
+#pragma unroll
+  for (int k8 = 0; k8 < 8; ++k8) am8[k8] = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; i += 2)
+    am8[(i >> 1) & 7] = max3(am8[(i >> 1) & 7], fabsf(__uint_as_float(r[i])), fabsf(__uint_as_float(r[i + 1])));
+  return fmaxf(fmaxf(fmaxf(am8[0], am8[1]), fmaxf(am8[2], am8[3])),
+               fmaxf(fmaxf(am8[4], am8[5]), fmaxf(am8[6], am8[7])));
+}
+
 // Visible key range [lo, hi] of the query at absolute position q_abs
 // (lower-right causal, local window), clipped to [0, k_len).
 struct KeyRange { int lo, hi; };

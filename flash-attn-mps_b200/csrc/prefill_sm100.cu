@@ -443,6 +443,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sl2e = ALIBI ? 1.f : sl2;
       const float cap_l2 = p.softcap * 1.4426950408889634f;  // softcap: cap*log2e*tanh(s*scale/cap)
       const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
+      // Scores up to this magnitude take the softcap's FMA-pipe polynomial.
+      const float cap_lim = SOFTCAP ? softcap_poly_limit(cap_in) : -1.f;
       // Running max in log2 units; a sink acts as one extra logit with zero value.
       float m_run = p.sinks ? load_float(p.sinks, p.sink_t, h * p.si0) * 1.4426950408889634f : -INFINITY;
       float l_run = p.sinks ? 1.f : 0.f;
@@ -465,6 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32_at<96>(tS + 96, r);
         }
         tmem_wait_ld();
+        // Softcap route for this tile, uniform over the warp: the polynomial
+        // tanh when every raw score of the warp's 32 rows (masked columns
+        // included) has |s * scale / cap| <= 3/4, else the identity route.
+        bool cap_poly = false;
+        if constexpr (SOFTCAP) cap_poly = __all_sync(0xffffffffu, row_absmax(r) <= cap_lim);
         if (!(ALIBI && SOFTCAP) && need_mask) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
@@ -472,33 +479,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if constexpr (ALIBI && SOFTCAP) {
           // v = cap*log2e*tanh(s*scale/cap) - slope*log2e*|q_abs - key| (the
-          // reference's capped score minus the ALiBi bias, in log2 units), with
+          // reference's capped score minus the ALiBi bias, in log2 units):
+          // in one pass with the polynomial tanh, or with
           // tanh(y) = 1 - 2/(e^(2y)+1) as in the softcap-only stage below, in
           // two in-place passes over the row; then the mask.
-          const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
-          {
-            const Exp2Poly<false> tanh_poly;
+          const float base = (float)(q_abs - key0);
+          const uint64_t nslope2 = f2pack(-slope_l2, -slope_l2);
+          if (cap_poly) {
+            const TanhPoly tpoly(sl2, cap_in);
 #pragma unroll
             for (int i = 0; i < BN; i += 2) {
-              float u0, u1, e0, e1;
-              f2unpack(fmul2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), tanh_k2), u0, u1);
-              tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
-              r[i] = __float_as_uint(e0);
-              r[i + 1] = __float_as_uint(e1);
+              const uint64_t dist2 = f2pack(fabsf(base - (float)i), fabsf(base - (float)(i + 1)));
+              float v0, v1;
+              f2unpack(tpoly.fma(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), fmul2(dist2, nslope2)),
+                       v0, v1);
+              r[i] = __float_as_uint(v0);
+              r[i + 1] = __float_as_uint(v1);
             }
-          }
-          const float base = (float)(q_abs - key0);
-          const uint64_t nslope2 = f2pack(-slope_l2, -slope_l2), cap_l2x2 = f2pack(cap_l2, cap_l2);
-          const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f);
+          } else {
+            const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
+            {
+              const Exp2Poly<false> tanh_poly;
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) {
-            float d0, d1, v0, v1;
-            f2unpack(fadd2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), one2), d0, d1);
-            const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
-            const uint64_t dist2 = f2pack(fabsf(base - (float)i), fabsf(base - (float)(i + 1)));
-            f2unpack(ffma2(t2, cap_l2x2, fmul2(dist2, nslope2)), v0, v1);
-            r[i] = __float_as_uint(v0);
-            r[i + 1] = __float_as_uint(v1);
+              for (int i = 0; i < BN; i += 2) {
+                float u0, u1, e0, e1;
+                f2unpack(fmul2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), tanh_k2), u0, u1);
+                tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
+                r[i] = __float_as_uint(e0);
+                r[i + 1] = __float_as_uint(e1);
+              }
+            }
+            const uint64_t cap_l2x2 = f2pack(cap_l2, cap_l2);
+            const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f);
+#pragma unroll
+            for (int i = 0; i < BN; i += 2) {
+              float d0, d1, v0, v1;
+              f2unpack(fadd2(f2pack(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), one2), d0, d1);
+              const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
+              const uint64_t dist2 = f2pack(fabsf(base - (float)i), fabsf(base - (float)(i + 1)));
+              f2unpack(ffma2(t2, cap_l2x2, fmul2(dist2, nslope2)), v0, v1);
+              r[i] = __float_as_uint(v0);
+              r[i + 1] = __float_as_uint(v1);
+            }
           }
           if (need_mask) {
 #pragma unroll
@@ -544,49 +566,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t ls2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
-        const uint64_t sl2x2 = f2pack(sl2e, sl2e), nmsub2 = f2pack(-msub, -msub);
-        // softcap constants: e^(2y) = 2^(s * cap_in * 2 log2e)
-        const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
-        const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
-        const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
-        const Exp2Poly<BF16> poly;  // degree 3 for bf16 P, 4 for f16 P
+        const uint64_t nmsub2 = f2pack(-msub, -msub);
+        // kMode 0: scores already scaled or biased; 1: softcap by the
+        // polynomial tanh; 2: softcap by the identity. The softcap tile takes
+        // one route for the whole warp (cap_poly), so the two loops never mix.
+        auto exp_stage = [&](auto mode) {
+          constexpr int kMode = decltype(mode)::value;
+          const uint64_t sl2x2 = f2pack(sl2e, sl2e);
+          // identity route: e^(2y) = 2^(s * cap_in * 2 log2e)
+          const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
+          const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
 #pragma unroll
-        for (int c8 = 0; c8 < BN / 16; ++c8) {
-          uint32_t pk[8];
+          for (int c8 = 0; c8 < BN / 16; ++c8) {
+            uint32_t pk[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float p0, p1;
-            const float s0 = __uint_as_float(r[c8 * 16 + 2 * i]), s1 = __uint_as_float(r[c8 * 16 + 2 * i + 1]);
-            if constexpr (CAP_IN_EXP) {
-              // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1):
-              // e^(2y) on the FMA pipe (degree-4 polynomial, argument clamped
-              // to +-64 where tanh is +-1 in fp32), one MUFU rcp, one MUFU ex2.
-              float u0, u1;
-              f2unpack(fmul2(f2pack(s0, s1), tanh_k2), u0, u1);
-              float e0, e1;
-              tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
-              float d0, d1;
-              f2unpack(fadd2(f2pack(e0, e1), one2), d0, d1);
-              const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
-              float l0, l1;
-              f2unpack(ffma2(t2, cap_l2x2, nmsub2), l0, l1);
-              p0 = s0 == -INFINITY ? 0.f : ex2(l0);
-              p1 = s1 == -INFINITY ? 0.f : ex2(l1);
-            } else {
-              const uint64_t x2 = ffma2(f2pack(s0, s1), sl2x2, nmsub2);
-              if (i >= 8 - kPolyPairs) {
-                poly(x2, p0, p1);  // FMA pipe
+            for (int i = 0; i < 8; ++i) {
+              float p0, p1;
+              const float s0 = __uint_as_float(r[c8 * 16 + 2 * i]), s1 = __uint_as_float(r[c8 * 16 + 2 * i + 1]);
+              if constexpr (kMode == 1) {
+                // cap*log2e*tanh(s*scale/cap) - m = s * R(s^2) - m on the FMA
+                // pipe, one MUFU ex2.
+                const TanhPoly tpoly(sl2, cap_in);
+                float l0, l1;
+                f2unpack(tpoly.fma(f2pack(s0, s1), nmsub2), l0, l1);
+                p0 = ex2(l0);  // a masked score gives l = -inf exactly: p = 0
+                p1 = ex2(l1);
+              } else if constexpr (kMode == 2) {
+                // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1):
+                // e^(2y) on the FMA pipe (degree-4 polynomial, argument clamped
+                // to +-64 where tanh is +-1 in fp32), one MUFU rcp, one MUFU ex2.
+                const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
+                float u0, u1;
+                f2unpack(fmul2(f2pack(s0, s1), tanh_k2), u0, u1);
+                float e0, e1;
+                tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
+                float d0, d1;
+                f2unpack(fadd2(f2pack(e0, e1), one2), d0, d1);
+                const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
+                float l0, l1;
+                f2unpack(ffma2(t2, cap_l2x2, nmsub2), l0, l1);
+                p0 = s0 == -INFINITY ? 0.f : ex2(l0);
+                p1 = s1 == -INFINITY ? 0.f : ex2(l1);
               } else {
-                float x0, x1;
-                f2unpack(x2, x0, x1);
-                p0 = ex2(x0);  // MUFU
-                p1 = ex2(x1);
+                const uint64_t x2 = ffma2(f2pack(s0, s1), sl2x2, nmsub2);
+                if (i >= 8 - kPolyPairs) {
+                  const Exp2Poly<BF16> poly;  // degree 3 for bf16 P, 4 for f16 P
+                  poly(x2, p0, p1);  // FMA pipe
+                } else {
+                  float x0, x1;
+                  f2unpack(x2, x0, x1);
+                  p0 = ex2(x0);  // MUFU
+                  p1 = ex2(x1);
+                }
               }
+              ls2[i & 3] = fadd2(ls2[i & 3], f2pack(p0, p1));
+              pk[i] = pack_p<BF16>(p0, p1);
             }
-            ls2[i & 3] = fadd2(ls2[i & 3], f2pack(p0, p1));
-            pk[i] = pack_p<BF16>(p0, p1);
+            tmem_st8_at<0>(tS + c8 * 8, pk);
           }
-          tmem_st8_at<0>(tS + c8 * 8, pk);
+        };
+        if constexpr (CAP_IN_EXP) {
+          if (cap_poly) exp_stage(std::integral_constant<int, 1>());
+          else exp_stage(std::integral_constant<int, 2>());
+        } else {
+          exp_stage(std::integral_constant<int, 0>());
         }
         // Lazy O rescale (after the exponentials, while S no longer occupies
         // registers). PV(j) is issued only after this row's P-ready arrival.

@@ -377,6 +377,8 @@ __global__ void __launch_bounds__(kWThreads, 1)
       const float sl2 = qk_scale * 1.4426950408889634f;     // raw score -> log2 units
       const float cap_l2 = p.softcap * 1.4426950408889634f;  // softcap: cap*log2e*tanh(s*scale/cap)
       const float cap_in = SOFTCAP ? qk_scale / p.softcap : 0.f;
+      // Scores up to this magnitude take the softcap's FMA-pipe polynomial.
+      const float cap_lim = SOFTCAP ? softcap_poly_limit(cap_in) : -1.f;
       // Running max in log2 units; a sink acts as one extra logit with zero value.
       float m_run = p.sinks ? load_float(p.sinks, p.sink_t, h * p.si0) * 1.4426950408889634f : -INFINITY;
       float l_run = p.sinks ? 1.f : 0.f;
@@ -397,6 +399,11 @@ __global__ void __launch_bounds__(kWThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(W_SC));
+        // Softcap route for this tile, uniform over the warp: the polynomial
+        // tanh when every raw score of the warp's 32 rows (masked columns
+        // included) has |s * scale / cap| <= 3/4, else the identity route.
+        bool cap_poly = false;
+        if constexpr (SOFTCAP) cap_poly = __all_sync(0xffffffffu, row_absmax(r) <= cap_lim);
         if (need_mask) {
 #pragma unroll
           for (int i = 0; i < BN; ++i)
@@ -425,36 +432,55 @@ __global__ void __launch_bounds__(kWThreads, 1)
         uint64_t ls2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) ls2[i] = f2pack(0.f, 0.f);
-        const uint64_t sl2x2 = f2pack(sl2, sl2), nmsub2 = f2pack(-msub, -msub);
-        const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
-        const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
-        const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
+        const uint64_t nmsub2 = f2pack(-msub, -msub);
         uint32_t pk[BN / 2];
+        // kMode 0: plain scores; 1: softcap by the polynomial tanh; 2: softcap
+        // by the identity (one route per warp and tile, see cap_poly).
+        auto exp_stage = [&](auto mode) {
+          constexpr int kMode = decltype(mode)::value;
+          const uint64_t sl2x2 = f2pack(sl2, sl2);
+          const uint64_t tanh_k2 = f2pack(cap_in * 2.8853900817779268f, cap_in * 2.8853900817779268f);
+          const uint64_t one2 = f2pack(1.f, 1.f), neg_two2 = f2pack(-2.f, -2.f), cap_l2x2 = f2pack(cap_l2, cap_l2);
 #pragma unroll
-        for (int i = 0; i < BN / 2; ++i) {
-          float p0, p1;
-          const float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
-          if constexpr (SOFTCAP) {
-            // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1).
-            float u0, u1;
-            f2unpack(fmul2(f2pack(s0, s1), tanh_k2), u0, u1);
-            float e0, e1;
-            tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
-            float d0, d1;
-            f2unpack(fadd2(f2pack(e0, e1), one2), d0, d1);
-            const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
-            float l0, l1;
-            f2unpack(ffma2(t2, cap_l2x2, nmsub2), l0, l1);
-            p0 = s0 == -INFINITY ? 0.f : ex2(l0);
-            p1 = s1 == -INFINITY ? 0.f : ex2(l1);
-          } else {
-            float x0, x1;
-            f2unpack(ffma2(f2pack(s0, s1), sl2x2, nmsub2), x0, x1);
-            p0 = ex2(x0);
-            p1 = ex2(x1);
+          for (int i = 0; i < BN / 2; ++i) {
+            float p0, p1;
+            const float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
+            if constexpr (kMode == 1) {
+              // cap*log2e*tanh(s*scale/cap) - m by the polynomial, one MUFU ex2.
+              const TanhPoly tpoly(sl2, cap_in);
+              float l0, l1;
+              f2unpack(tpoly.fma(f2pack(s0, s1), nmsub2), l0, l1);
+              p0 = ex2(l0);  // a masked score gives l = -inf exactly: p = 0
+              p1 = ex2(l1);
+            } else if constexpr (kMode == 2) {
+              // cap*log2e*tanh(s*scale/cap) - m with tanh(y) = 1 - 2/(e^(2y)+1).
+              const Exp2Poly<false> tanh_poly;  // degree 4: tanh error ~3e-6
+              float u0, u1;
+              f2unpack(fmul2(f2pack(s0, s1), tanh_k2), u0, u1);
+              float e0, e1;
+              tanh_poly.in_range(f2pack(fminf(fmaxf(u0, -64.f), 64.f), fminf(fmaxf(u1, -64.f), 64.f)), e0, e1);
+              float d0, d1;
+              f2unpack(fadd2(f2pack(e0, e1), one2), d0, d1);
+              const uint64_t t2 = ffma2(f2pack(rcp(d0), rcp(d1)), neg_two2, one2);
+              float l0, l1;
+              f2unpack(ffma2(t2, cap_l2x2, nmsub2), l0, l1);
+              p0 = s0 == -INFINITY ? 0.f : ex2(l0);
+              p1 = s1 == -INFINITY ? 0.f : ex2(l1);
+            } else {
+              float x0, x1;
+              f2unpack(ffma2(f2pack(s0, s1), sl2x2, nmsub2), x0, x1);
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            ls2[i & 3] = fadd2(ls2[i & 3], f2pack(p0, p1));
+            pk[i] = pack_p<BF16>(p0, p1);
           }
-          ls2[i & 3] = fadd2(ls2[i & 3], f2pack(p0, p1));
-          pk[i] = pack_p<BF16>(p0, p1);
+        };
+        if constexpr (SOFTCAP) {
+          if (cap_poly) exp_stage(std::integral_constant<int, 1>());
+          else exp_stage(std::integral_constant<int, 2>());
+        } else {
+          exp_stage(std::integral_constant<int, 0>());
         }
         // The previous PV must have read its P and added into O before P is
         // replaced and O rescaled.
