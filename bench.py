@@ -48,12 +48,19 @@ def load_peaks():
 
 
 # --------------------------------------------------------------------- clocks
+# Host-time windows (time.monotonic() before the first timed launch, after the
+# synchronize that ends the timed region) of every timed region so far; the
+# clock record of a measurement keeps the samples taken inside its windows.
+TIMED_WINDOWS = []
+
+
 class ClockSampler:
     """SM clocks and throttle reasons sampled while a measurement runs
-    (read-only). In-process NVML reads every 20 ms, so that timed regions of
-    tens of milliseconds still get several samples; `nvidia-smi -lms 200` when
-    NVML is unavailable. The device is the torch device `index`, matched to
-    NVML by PCI bus id."""
+    (read-only). In-process NVML reads every 5 ms, timestamped, so that a timed
+    region of tens of milliseconds still gets several samples and the record
+    can be limited to the timed windows; `nvidia-smi -lms 200` when NVML is
+    unavailable. The device is the torch device `index`, matched to NVML by
+    PCI bus id."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -63,13 +70,13 @@ class ClockSampler:
     REASONS = (("hw_slowdown", 0x8 | 0x80), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
                ("sw_power_cap", 0x4))
 
-    def __init__(self, index, period_s=0.02):
+    def __init__(self, index, period_s=0.005):
         self.index = index
         self.period = period_s
         self.proc = None
         self.thread = None
         self.lines = []
-        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.samples = []  # (host time, sm_mhz, reasons bitmask)
         self.smax = None
         self.stop_flag = threading.Event()
         self.source = None
@@ -96,14 +103,14 @@ class ClockSampler:
                     try:
                         sm = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
                         rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
-                        self.samples.append((float(sm), int(rs)))
+                        self.samples.append((time.monotonic(), float(sm), int(rs)))
                     except Exception:
                         pass
                     self.stop_flag.wait(self.period)
 
             self.thread = threading.Thread(target=poll, daemon=True)
             self.thread.start()
-            self.source = "nvml 20 ms"
+            self.source = "nvml 5 ms"
             return
         except Exception:
             self.thread = None
@@ -122,16 +129,31 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def stop(self):
+    @staticmethod
+    def in_windows(samples, windows):
+        """The samples taken inside any of the host-time windows."""
+        return [x for x in samples if any(t0 <= x[0] <= t1 for t0, t1 in windows)]
+
+    def stop(self, windows=None):
+        """Median SM clock and the throttle reasons seen. With ``windows``
+        (host-time spans of the timed regions) only samples inside them count;
+        if none fell inside, all samples of the run are reported and
+        ``timed_windows_only`` is false."""
         if self.source is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock source"], "samples": 0}
         if self.proc is None:
             self.stop_flag.set()
             self.thread.join(timeout=2)
-            sm = [x for x, _ in self.samples]
-            reasons = sorted({name for _, mask in self.samples for name, bit in self.REASONS if mask & bit})
-            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
-                    "reasons": reasons, "samples": len(sm), "source": self.source}
+            inside = self.in_windows(self.samples, windows) if windows else []
+            use = inside or self.samples
+            sm = [x for _, x, _ in use]
+            reasons = sorted({name for _, _, mask in use for name, bit in self.REASONS if mask & bit})
+            out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                   "reasons": reasons, "samples": len(sm), "source": self.source}
+            if windows:
+                out["timed_windows_only"] = bool(inside)
+                out["timed_s"] = round(sum(t1 - t0 for t0, t1 in windows), 4)
+            return out
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -383,11 +405,13 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     barrier(world)
     from flash_attn_b200._capi import kernel_launches
     launches_before = kernel_launches()
+    t0 = time.monotonic()
     start.record(stream)
     for _ in range(args.steps):
         step(q)
     end.record(stream)
     barrier(world)
+    windows = [(t0, time.monotonic())]
     launches = kernel_launches() - launches_before
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms, world)
@@ -395,6 +419,7 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
     # ---- dominant kernel alone: the local decode operation (decode + split merge)
     k_start, k_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
+    t0 = time.monotonic()
     k_start.record(stream)
     for _ in range(args.steps):
         attention(q, k_cache, v_cache, cu_seqlens_q=cu_q, seqused_k=used, max_seqlen_q=1,
@@ -402,8 +427,9 @@ def run_fp8_decode(args, rank, world, peaks, peak_kind):
                   out=partial if world > 1 else out)
     k_end.record(stream)
     barrier(world)
+    windows.append((t0, time.monotonic()))
     kernel_ms = max_over_ranks(k_start.elapsed_time(k_end) / args.steps, world)
-    clocks = sampler.stop() if sampler else None
+    clocks = sampler.stop(windows) if sampler else None
 
     # ---- end to end through the public API with host buffers ----------------
     new_k_host = torch.randn(B, HK, D, generator=gq).to(torch.bfloat16).pin_memory()
@@ -544,8 +570,9 @@ def rested(measure, pause=2.0):
     time.sleep(pause)
     sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
+    first = len(TIMED_WINDOWS)
     result = measure()
-    result["clocks"] = sampler.stop()
+    result["clocks"] = sampler.stop(TIMED_WINDOWS[first:])
     return result
 
 
@@ -569,11 +596,13 @@ def time_loop(fn, steps, warmup, min_seconds=0.0):
         torch.cuda.synchronize()
         est = max(s.elapsed_time(e) / 3, 1e-3)
         steps = max(steps, int(min_seconds * 1e3 / est) + 1)
+    t0 = time.monotonic()
     s.record(stream)
     for _ in range(steps):
         fn()
     e.record(stream)
     torch.cuda.synchronize()
+    TIMED_WINDOWS.append((t0, time.monotonic()))
     ms = s.elapsed_time(e) / steps
     return (ms, steps) if min_seconds > 0 else ms
 
@@ -903,9 +932,10 @@ def run_serving(peaks, peak_kind, steps=2, warmup=3, small=False, path="fused", 
     sampler = ClockSampler(torch.cuda.current_device())
     sampler.start()
     time.sleep(0.3)
+    first = len(TIMED_WINDOWS)
     ms = time_loop(lambda: loop(prompts), steps, 0)
     prefill_ms = time_loop(lambda: engine.prefill(list(prompts.unbind(0))), steps, 1)
-    clocks = sampler.stop()
+    clocks = sampler.stop(TIMED_WINDOWS[first:])
 
     def e2e_loop():
         prompts.copy_(prompts_host, non_blocking=True)
